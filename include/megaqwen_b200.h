@@ -1,0 +1,170 @@
+/*
+ * megaqwen_b200.h -- C ABI of the B200 (sm_100a) Qwen3-0.6B decode library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t and
+ * returns an int status: 0 on success, a negative MQ_ERR_* code on a host-side
+ * validation failure, or a positive cudaError_t value when a CUDA call failed.
+ * Nothing here takes a torch type.  Errors detected on the device (a bounded
+ * wait that ran out) are reported through mq_device_status().
+ *
+ * The struct layouts below keep the field order of the reference's layout
+ * contract (config.cuh:45-67 in Yunle-Lee/MegaQwen-A10) so that a pointer table
+ * built for the reference can be passed unchanged.
+ */
+#ifndef MEGAQWEN_B200_H
+#define MEGAQWEN_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Per-layer weight pointers, field order of config.cuh:45-57.  For the INT8
+ * decoder the seven projection pointers point at int8 [out,in] row-major
+ * codes; for the BF16 decoder at bf16 [out,in].  Norm weights are bf16. */
+typedef struct LayerWeights {
+    const void* input_layernorm_weight;
+    const void* q_proj_weight;
+    const void* k_proj_weight;
+    const void* v_proj_weight;
+    const void* q_norm_weight;
+    const void* k_norm_weight;
+    const void* o_proj_weight;
+    const void* post_attn_layernorm_weight;
+    const void* gate_proj_weight;
+    const void* up_proj_weight;
+    const void* down_proj_weight;
+} LayerWeights;
+
+/* Per-layer fp32 per-output-channel scales, field order of config.cuh:59-67. */
+typedef struct ScalePointers {
+    float* q_scale;
+    float* k_scale;
+    float* v_scale;
+    float* o_scale;
+    float* gate_scale;
+    float* up_scale;
+    float* down_scale;
+} ScalePointers;
+
+enum {
+    MQ_OK = 0,
+    MQ_ERR_ARG = -1,        /* null pointer, bad size or misaligned pointer */
+    MQ_ERR_TOKEN = -2,      /* token id outside [0, vocab) */
+    MQ_ERR_POSITION = -3,   /* position outside [0, max_seq_len) or cache_len != position+1 */
+    MQ_ERR_DEVICE = -4,     /* device has too few SMs / shared memory for the kernel */
+    MQ_ERR_SIZE = -5        /* a size is larger than the entry point supports */
+};
+
+/* Device-side status codes written by the decode kernel (mq_device_status). */
+enum {
+    MQ_DEV_OK = 0,
+    MQ_DEV_TIMEOUT_EXCHANGE = 1,  /* a tagged-word exchange wait ran out */
+    MQ_DEV_TIMEOUT_RING = 2,      /* a weight-ring mbarrier wait ran out */
+    MQ_DEV_BAD_TOKEN = 3          /* on-device token feedback produced an invalid id */
+};
+
+/*
+ * INT8 weight-only fused decode step.  Replaces launch_a10_int8_decode
+ * (a10_int8_decode_kernel.cu:821-842; declared for the torch wrapper at
+ * bench_int8.py:97-117) with the same argument names and order.
+ *   - runs one greedy decode step at `position` (cache_len must equal
+ *     position+1), writes K/V for `position` into k_cache/v_cache
+ *     ([num_layers][8][max_seq_len][128] bf16), writes the final RMSNorm output
+ *     to g_normalized (fp32[1024]) and the argmax token to *output_token_id
+ *     (device int32).
+ *   - hidden_buffer, g_activations, g_residual, g_q, g_k, g_v, g_attn_out,
+ *     g_mlp_intermediate, block_max_vals and block_max_idxs are accepted for
+ *     signature compatibility and not written: the kernel keeps its hand-off
+ *     state in a library-owned per-device workspace.
+ *   - returns a status instead of void.
+ */
+int launch_a10_int8_decode(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale,
+    const void* cos_table, const void* sin_table,
+    void* k_cache, void* v_cache, void* hidden_buffer,
+    void* g_activations, void* g_residual, void* g_q, void* g_k, void* g_v,
+    void* g_attn_out, void* g_mlp_intermediate, void* g_normalized,
+    void* block_max_vals, void* block_max_idxs,
+    int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
+    const ScalePointers* scales, cudaStream_t stream);
+
+/* BF16 fused decode step.  Replaces launch_a10_decode
+ * (a10_decode_kernel.cu:761-780): same arguments as the INT8 entry point minus
+ * lm_head_scale and scales; weights are bf16. */
+int launch_a10_decode(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    const void* cos_table, const void* sin_table,
+    void* k_cache, void* v_cache, void* hidden_buffer,
+    void* g_activations, void* g_residual, void* g_q, void* g_k, void* g_v,
+    void* g_attn_out, void* g_mlp_intermediate, void* g_normalized,
+    void* block_max_vals, void* block_max_idxs,
+    int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
+    cudaStream_t stream);
+
+/*
+ * Multi-step decode with on-device token feedback (no reference counterpart:
+ * the reference runs one launch plus one .item() per token,
+ * bench_int8.py:193-219).  Runs `num_steps` greedy steps starting at
+ * `position`; the first input token is *d_token_in (device int32), each later
+ * input is the previous step's argmax.  Token j is written to d_tokens_out[j].
+ * weight_kind: 0 = INT8 (lm_head_scale and scales required), 1 = BF16.
+ * d_logits (optional, may be NULL): fp32[151936] logits of the LAST step.
+ * d_layer_hidden (optional, may be NULL): fp32[num_layers][1024], the bf16
+ *   residual stream after each layer of the LAST step (diagnostics/parity).
+ */
+int mq_decode_multi(
+    int weight_kind, const int* d_token_in, int* d_tokens_out, int num_steps,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale,
+    const ScalePointers* scales, const void* cos_table, const void* sin_table,
+    void* k_cache, void* v_cache, float* g_normalized, float* d_logits, float* d_layer_hidden,
+    int num_layers, int position, int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/*
+ * Per-output-channel symmetric INT8 quantizer.  Same arithmetic as
+ * quantize_per_channel (bench_int8.py:19-24): absmax in bf16,
+ * scale = fp32(bf16(absmax/127)) clamped to >= 1e-12,
+ * q = clamp(round_half_even(fp32(w)/scale), -128, 127).
+ * w: bf16 [M,K] row-major; q: int8 [M,K]; scale: fp32 [M].
+ */
+int mq_quantize_per_channel(const void* w_bf16, int64_t M, int64_t K,
+                            int8_t* q_out, float* scale_out, cudaStream_t stream);
+
+/*
+ * Standalone weight-only matvec, y[m] = scale[m] * sum_k W[m,k] * x[k]
+ * (the per-projection math of a10_int8_decode_kernel.cu:87-136 and
+ * int8_gemv, int8_decoder.py:100-115).  weight_kind 0 = int8 W with fp32
+ * scale, 1 = bf16 W (scale ignored, may be NULL).  x, y fp32 on the device.
+ * K must be one of 1024, 2048, 3072.
+ */
+int mq_matvec(int weight_kind, const void* W, const float* scale, const float* x,
+              float* y, int M, int K, cudaStream_t stream);
+
+/* Reads (and with clear != 0, clears) the device-side status of this device's
+ * decode workspace.  Synchronises the device.  *code gets an MQ_DEV_* value,
+ * *info the kernel's location code for it. */
+int mq_device_status(int* code, int* info, int clear);
+
+/* Sets the bounded-wait budget (nanoseconds) that every spin in the decode
+ * kernel uses before it gives up with MQ_DEV_TIMEOUT_*.  Default 2e9. */
+int mq_set_wait_budget_ns(uint64_t ns);
+
+/* Test hook: when nonzero, the next decode launch's CTA `cta` skips writing
+ * its share of the QKV exchange, so every consumer of it runs into the
+ * bounded wait and reports MQ_DEV_TIMEOUT_EXCHANGE.  Cleared after one launch. */
+int mq_inject_skip_publish(int enable, int cta);
+
+/* Number of CTAs (one per SM) and dynamic shared memory the decode kernel uses. */
+int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,163 @@
+// common.cuh -- shapes, launch geometry and device primitives shared by the
+// sm_100a kernels of this library.
+//
+// Model shapes are the Qwen3-0.6B constants of the reference's config.cuh:30-40.
+// The launch geometry is B200-specific: one persistent CTA per SM (148 on B200),
+// NCW consumer warps plus one producer warp that streams weights and KV rows
+// into a shared-memory ring with cp.async.bulk (non-multicast, local HBM only).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include "../../include/megaqwen_b200.h"
+
+namespace mq {
+
+constexpr int HIDDEN = 1024;
+constexpr int INTER = 3072;
+constexpr int NQH = 16;
+constexpr int NKVH = 8;
+constexpr int HD = 128;
+constexpr int QSZ = NQH * HD;        // 2048
+constexpr int KVSZ = NKVH * HD;      // 1024
+constexpr int QKV_ROWS = QSZ + 2 * KVSZ;  // 4096
+constexpr int VOCAB = 151936;
+constexpr float RMS_EPS = 1e-6f;
+
+constexpr int NCW = 12;                       // consumer warps
+constexpr int NCT = NCW * 32;                 // consumer threads
+constexpr int NTHREADS = NCT + 32;            // + producer warp
+constexpr int STAGE_BYTES = 16384;
+constexpr int NSTAGE = 11;
+constexpr int KV_CHUNK_POS = STAGE_BYTES / (2 * HD * 2);  // 32 positions of K then V
+constexpr int MAX_SPLITS = 18;                // attention splits per KV head
+
+// ---------------------------------------------------------------------------
+// Tagged hand-off words.  A value crossing CTAs is published as one 64-bit
+// store (tag << 32 | payload).  An aligned 64-bit store is single-copy atomic,
+// so a consumer that reads the expected tag also reads the matching payload;
+// no fence or grid barrier is needed on the critical path.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_tagged(uint64_t* p, uint32_t tag, uint32_t payload) {
+    uint64_t v = ((uint64_t)tag << 32) | payload;
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_relaxed32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk copy (TMA engine, untiled, no multicast)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) { return __uint_as_float(b16 << 16); }
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Orderable key for a float: larger float -> larger unsigned key.
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// Weight-type traits: how many elements a 16-byte unit holds and how to
+// accumulate a unit against fp32 activations held in registers.
+// ---------------------------------------------------------------------------
+struct W8 {
+    static constexpr int EPU = 16;  // int8 elements per 16-byte unit
+    static constexpr bool HAS_SCALE = true;
+    // int8 -> fp32 exactly: byte^0x80 placed in the mantissa of 2^23, minus 2^23+128.
+    __device__ __forceinline__ static void dot(const uint4 w, const float* x, float& a0, float& a1) {
+        const uint32_t ws[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
+                                w.w ^ 0x80808080u};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                float f = __uint_as_float(__byte_perm(ws[j], 0x4B000000u, 0x7650 | b)) - 8388736.f;
+                if (j & 1) a1 = fmaf(f, x[j * 4 + b], a1);
+                else a0 = fmaf(f, x[j * 4 + b], a0);
+            }
+        }
+    }
+};
+struct W16 {
+    static constexpr int EPU = 8;  // bf16 elements per 16-byte unit
+    static constexpr bool HAS_SCALE = false;
+    __device__ __forceinline__ static void dot(const uint4 w, const float* x, float& a0, float& a1) {
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float lo = __uint_as_float(ws[j] << 16);
+            float hi = __uint_as_float(ws[j] & 0xffff0000u);
+            if (j & 1) { a1 = fmaf(lo, x[2 * j], a1); a1 = fmaf(hi, x[2 * j + 1], a1); }
+            else       { a0 = fmaf(lo, x[2 * j], a0); a0 = fmaf(hi, x[2 * j + 1], a0); }
+        }
+    }
+};
+
+__host__ __device__ __forceinline__ int split_lo(int n, int parts, int i) {
+    return (int)(((long long)n * i) / parts);
+}
+
+}  // namespace mq

@@ -1,0 +1,73 @@
+// decode.cuh -- data structures of the persistent decode kernel.
+#pragma once
+#include "common.cuh"
+
+namespace mq {
+
+constexpr int PART_WORDS = 2 * HD + 4;  // acc[2][128], m[2], l[2] per attention split
+constexpr int TAGS_PER_LAYER = 8;
+
+// Library-owned per-device workspace.  Hand-off buffers are double-buffered by
+// layer parity; every word carries the epoch tag of the exchange that wrote it.
+struct Workspace {
+    uint32_t epoch;                 // tag base of the next launch
+    uint32_t exit_ctr;              // CTAs that finished the current launch
+    unsigned long long argmax;      // packed (order_key(logit) << 32 | ~row)
+    int err_code;                   // first MQ_DEV_* error of any launch since cleared
+    int err_info;                   // location code of that error
+    int pad_[10];
+    uint64_t xh[2][HIDDEN];         // residual stream h (bf16 payload), input of layer l
+    uint64_t xqkv[2][QKV_ROWS];     // raw q|k|v projections (fp32)
+    uint64_t xattn[2][QSZ];         // attention output per q head (fp32)
+    uint64_t xact[2][HIDDEN];       // h + O-proj (fp32)
+    uint64_t xmlp[2][INTER];        // silu(gate)*up (fp32)
+    uint64_t xpart[2][NKVH * MAX_SPLITS * PART_WORDS];  // split-K attention partials
+};
+
+struct DecodeParams {
+    const void* embed;
+    const LayerWeights* layers;     // device array [L]
+    const ScalePointers* scales;    // device array [L] (INT8 only)
+    const void* final_norm;
+    const void* lm_w;
+    const float* lm_scale;          // INT8 only
+    const __nv_bfloat16* cos_t;
+    const __nv_bfloat16* sin_t;
+    __nv_bfloat16* kc;
+    __nv_bfloat16* vc;
+    float* g_normalized;            // optional fp32[1024]
+    float* logits;                  // optional fp32[VOCAB]
+    float* layer_hidden;            // optional fp32[L][1024]
+    const int* token_in_dev;        // optional; else token_in
+    int* token_out;                 // device int32
+    Workspace* ws;
+    unsigned long long budget_ns;
+    int token_in;
+    int L;
+    int position;                   // cache_len = position + 1
+    int max_seq;
+    int splits;                     // attention splits per KV head
+    float attn_scale;
+    int skip_cta;                   // test hook: CTA that skips its layer-0 QKV publish (-1: none)
+};
+
+// Shared-memory layout (dynamic).
+struct Smem {
+    uint8_t ring[NSTAGE][STAGE_BYTES];
+    uint64_t full[NSTAGE];
+    uint64_t empty[NSTAGE];
+    float h[HIDDEN];         // residual stream (fp32 copy of bf16 h)
+    float act[HIDDEN];       // h + O (residual of the MLP half)
+    float x[INTER];          // current matvec activation (normalized / attn / mlp)
+    float red[NCW];
+    float raw[4 * HD];       // raw q0 q1 k v of this CTA's KV head
+    float q[2][HD];
+    float m[2], l[2], corr[2];
+    float sc[2][KV_CHUNK_POS];
+    float pe[2][KV_CHUNK_POS];
+    uint16_t kvcur[2][HD];   // current-position K and V, bf16
+    unsigned long long best[NCW];
+    int abort_flag;
+};
+
+}  // namespace mq

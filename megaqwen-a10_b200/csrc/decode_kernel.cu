@@ -1,0 +1,999 @@
+// decode_kernel.cu -- persistent fused Qwen3-0.6B decode step for B200 (sm_100a).
+//
+// One launch = one greedy decode step: embedding -> num_layers x {RMSNorm+QKV,
+// QK-norm+RoPE+KV write, attention, O+residual, post-norm+gate/up+SiLU,
+// down+residual} -> final RMSNorm -> LM head + argmax.  This is the computation
+// of the reference's a10_decode_kernel + lm_head_phase1/2
+// (a10_int8_decode_kernel.cu:621-815) re-designed for B200:
+//   * one CTA per SM (148), NCW consumer warps + 1 producer warp;
+//   * the producer streams this CTA's weight rows (and KV rows for its attention
+//     split) through an NSTAGE x 16 KB shared-memory ring with cp.async.bulk, so
+//     HBM reads run ahead of the data dependencies;
+//   * no grid.sync: each cross-CTA value is a tagged 64-bit word and a consumer
+//     polls exactly the words it needs (see common.cuh);
+//   * every norm is recomputed per CTA instead of by CTA 0 plus a barrier;
+//   * attention is split over positions (flash-decode) with an online softmax,
+//     one work item per (KV head, split), both GQA heads of a KV head at once;
+//   * the LM head runs inside the same launch and reduces its argmax with one
+//     packed 64-bit atomicMax per CTA.
+// Every spin is bounded by a %globaltimer budget; on expiry the kernel records
+// an MQ_DEV_* code in the workspace, drains its bulk copies and returns.
+#include "decode.cuh"
+#include <stdlib.h>
+
+namespace mq {
+
+struct Ctx {
+    Smem* sm;
+    Workspace* ws;
+    unsigned long long budget;
+};
+
+__device__ __noinline__ void record_error(Ctx& c, int code, int info) {
+    if (atomicCAS(&c.ws->err_code, 0, code) == 0) atomicExch(&c.ws->err_info, info);
+    *(volatile int*)&c.sm->abort_flag = 1;
+}
+
+__device__ __forceinline__ bool aborted(Ctx& c) {
+    if (*(volatile int*)&c.sm->abort_flag) return true;
+    if (ld_relaxed32((const uint32_t*)&c.ws->err_code) != 0) {
+        *(volatile int*)&c.sm->abort_flag = 1;
+        return true;
+    }
+    return false;
+}
+
+// Poll one tagged word until its tag matches.  Returns the payload; on abort or
+// timeout returns 0 (the caller's CTA then leaves at the next phase boundary).
+__device__ __forceinline__ uint32_t poll_word(Ctx& c, const uint64_t* p, uint32_t tag, int where) {
+    uint64_t v = ld_relaxed64(p);
+    if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+    unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        v = ld_relaxed64(p);
+        if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+        if ((it & 127) == 0) {
+            if (aborted(c)) return 0;
+            if (globaltimer() - t0 > c.budget) {
+                record_error(c, MQ_DEV_TIMEOUT_EXCHANGE, where);
+                return 0;
+            }
+        }
+    }
+}
+
+// `budget_mul` lets the producer wait longer than the consumers: a producer
+// stalled on a full ring is a consequence of a stalled consumer, whose own
+// timeout is the root cause worth recording.
+__device__ __forceinline__ bool mbar_wait(Ctx& c, uint64_t* b, uint32_t parity, int where, int budget_mul = 1) {
+    if (mbar_test(b, parity)) return true;
+    unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_test(b, parity)) return true;
+        if ((it & 63) == 0) {
+            if (aborted(c)) return false;
+            if (globaltimer() - t0 > c.budget * budget_mul) {
+                record_error(c, MQ_DEV_TIMEOUT_RING, where);
+                return false;
+            }
+        }
+    }
+}
+
+// Consumer-side barrier with an OR-reduction: every consumer thread gets the same
+// answer to "has any thread seen an abort".
+__device__ __forceinline__ bool consumers_sync_abort(Ctx& c) {
+    int mine = *(volatile int*)&c.sm->abort_flag;
+    int any;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.or.pred q, 1, %2, p; selp.s32 %0, 1, 0, q; }"
+        : "=r"(any)
+        : "r"(mine), "r"(NCT)
+        : "memory");
+    return any != 0;
+}
+__device__ __forceinline__ void consumers_sync() { named_bar(1, NCT); }
+
+// ---------------------------------------------------------------------------
+// Work geometry, shared by producer and consumers so both walk the same chunks.
+// ---------------------------------------------------------------------------
+struct Geo {
+    int nb, b;
+    int qkv0, qkv1, o0, o1, gu0, gu1, d0, d1, lm0, lm1;
+    int item, g, s, S;
+    int c;                  // cache_len
+    int past0, past1;       // cache positions this split reads from the cache
+    bool owner;             // split that holds the current position
+
+    __device__ void init(const DecodeParams& P) {
+        nb = gridDim.x;
+        b = blockIdx.x;
+        qkv0 = split_lo(QKV_ROWS, nb, b); qkv1 = split_lo(QKV_ROWS, nb, b + 1);
+        o0 = split_lo(HIDDEN, nb, b);     o1 = split_lo(HIDDEN, nb, b + 1);
+        gu0 = split_lo(INTER, nb, b);     gu1 = split_lo(INTER, nb, b + 1);
+        d0 = o0; d1 = o1;
+        lm0 = split_lo(VOCAB, nb, b);     lm1 = split_lo(VOCAB, nb, b + 1);
+        S = P.splits;
+        c = P.position + 1;
+        const int nitems = NKVH * S;
+        const int stride = nb / nitems;
+        item = (b % stride == 0 && b / stride < nitems) ? b / stride : -1;
+        if (item >= 0) {
+            g = item / S;
+            s = item % S;
+            int p0 = split_lo(c, S, s), p1 = split_lo(c, S, s + 1);
+            owner = (s == S - 1);
+            past0 = p0;
+            past1 = owner ? c - 1 : p1;
+        } else {
+            g = s = 0; owner = false; past0 = past1 = 0;
+        }
+    }
+};
+
+template <class WT>
+struct Bytes {
+    static constexpr int ESZ = 16 / WT::EPU;  // bytes per weight element
+};
+
+// ---------------------------------------------------------------------------
+// Producer: one thread walks the CTA's chunk sequence for the whole step.
+// ---------------------------------------------------------------------------
+struct Producer {
+    Smem* sm;
+    uint32_t seq;
+
+    __device__ bool begin(Ctx& c, uint32_t bytes, uint8_t*& dst) {
+        const uint32_t stage = seq % NSTAGE, use = seq / NSTAGE;
+        if (use > 0 && !mbar_wait(c, &sm->empty[stage], (use - 1) & 1, 100 + (int)stage, 2)) return false;
+        mbar_arrive_expect_tx(&sm->full[stage], bytes);
+        dst = sm->ring[stage];
+        return true;
+    }
+    __device__ void end() { ++seq; }
+
+    // rows [a, b) of a row-major matrix with `rb` bytes per row.
+    __device__ bool rows(Ctx& c, const uint8_t* base, int a, int b, int rb) {
+        const int rpc = STAGE_BYTES / rb;
+        for (int r = a; r < b; r += rpc) {
+            const int n = min(rpc, b - r);
+            uint8_t* dst;
+            if (!begin(c, n * rb, dst)) return false;
+            bulk_g2s(dst, base + (size_t)r * rb, n * rb, &sm->full[seq % NSTAGE]);
+            end();
+        }
+        return true;
+    }
+};
+
+template <class WT>
+__device__ void producer_main(const DecodeParams& P, Ctx& c, const Geo& G) {
+    constexpr int ESZ = Bytes<WT>::ESZ;
+    Producer pr{c.sm, 0};
+    bool ok = true;
+    for (int l = 0; l < P.L && ok; ++l) {
+        const LayerWeights& w = P.layers[l];
+        // QKV rows in the stacked [q; k; v] row space.
+        {
+            const int rb = HIDDEN * ESZ, rpc = STAGE_BYTES / rb;
+            for (int r = G.qkv0; r < G.qkv1 && ok; r += rpc) {
+                const int n = min(rpc, G.qkv1 - r);
+                uint8_t* dst;
+                if (!(ok = pr.begin(c, n * rb, dst))) break;
+                uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
+                int done = 0;
+                while (done < n) {
+                    const int row = r + done;
+                    const uint8_t* src;
+                    int lim;
+                    if (row < QSZ) { src = (const uint8_t*)w.q_proj_weight + (size_t)row * rb; lim = QSZ; }
+                    else if (row < QSZ + KVSZ) { src = (const uint8_t*)w.k_proj_weight + (size_t)(row - QSZ) * rb; lim = QSZ + KVSZ; }
+                    else { src = (const uint8_t*)w.v_proj_weight + (size_t)(row - QSZ - KVSZ) * rb; lim = QKV_ROWS; }
+                    const int m = min(n - done, lim - row);
+                    bulk_g2s(dst + done * rb, src, m * rb, bar);
+                    done += m;
+                }
+                pr.end();
+            }
+        }
+        // KV rows of this CTA's attention split (positions written by earlier launches).
+        if (ok && G.item >= 0) {
+            const size_t head_off = ((size_t)l * NKVH + G.g) * (size_t)P.max_seq * HD;
+            for (int p = G.past0; p < G.past1 && ok; p += KV_CHUNK_POS) {
+                const int n = min(KV_CHUNK_POS, G.past1 - p);
+                uint8_t* dst;
+                if (!(ok = pr.begin(c, 2 * n * HD * 2, dst))) break;
+                uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
+                bulk_g2s(dst, P.kc + head_off + (size_t)p * HD, n * HD * 2, bar);
+                bulk_g2s(dst + KV_CHUNK_POS * HD * 2, P.vc + head_off + (size_t)p * HD, n * HD * 2, bar);
+                pr.end();
+            }
+        }
+        if (ok) ok = pr.rows(c, (const uint8_t*)w.o_proj_weight, G.o0, G.o1, QSZ * ESZ);
+        // gate/up: a chunk holds n gate rows followed by the same n up rows.
+        if (ok) {
+            const int rb = HIDDEN * ESZ, rpc = STAGE_BYTES / (2 * rb);
+            for (int r = G.gu0; r < G.gu1 && ok; r += rpc) {
+                const int n = min(rpc, G.gu1 - r);
+                uint8_t* dst;
+                if (!(ok = pr.begin(c, 2 * n * rb, dst))) break;
+                uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
+                bulk_g2s(dst, (const uint8_t*)w.gate_proj_weight + (size_t)r * rb, n * rb, bar);
+                bulk_g2s(dst + n * rb, (const uint8_t*)w.up_proj_weight + (size_t)r * rb, n * rb, bar);
+                pr.end();
+            }
+        }
+        if (ok) ok = pr.rows(c, (const uint8_t*)w.down_proj_weight, G.d0, G.d1, INTER * ESZ);
+    }
+    if (ok) pr.rows(c, (const uint8_t*)P.lm_w, G.lm0, G.lm1, HIDDEN * ESZ);
+    // Drain: never leave a bulk copy in flight into shared memory at exit.
+    const uint32_t first = pr.seq > (uint32_t)NSTAGE ? pr.seq - NSTAGE : 0u;
+    for (uint32_t q = first; q < pr.seq; ++q) {
+        const uint32_t stage = q % NSTAGE;
+        unsigned long long t0 = globaltimer();
+        while (!mbar_test(&c.sm->full[stage], (q / NSTAGE) & 1)) {
+            if (globaltimer() - t0 > c.budget) break;
+        }
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// Consumer side
+// ---------------------------------------------------------------------------
+struct Cons {
+    Smem* sm;
+    uint32_t seq;
+    int warp, lane, tid;
+
+    __device__ const uint8_t* wait(Ctx& c, int where) {
+        const uint32_t stage = seq % NSTAGE;
+        mbar_wait(c, &sm->full[stage], (seq / NSTAGE) & 1, where);
+        return sm->ring[stage];
+    }
+    __device__ void release() {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->empty[seq % NSTAGE]);
+        ++seq;
+    }
+};
+
+// Matvec over rows [r0, r1) of one projection streamed through the ring.
+// Row i (phase-relative) is handled by warp i % NCW; lane holds the activation
+// elements of its fixed 16-byte units in registers for the whole phase.
+template <class WT, int K, class Out>
+__device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Out out) {
+    constexpr int ESZ = Bytes<WT>::ESZ;
+    constexpr int RB = K * ESZ;
+    constexpr int UPL = K / (WT::EPU * 32);
+    constexpr int RPC = STAGE_BYTES / RB;
+    float xr[UPL * WT::EPU];
+#pragma unroll
+    for (int j = 0; j < UPL; ++j) {
+        const int e0 = (cs.lane + 32 * j) * WT::EPU;
+#pragma unroll
+        for (int e = 0; e < WT::EPU; e += 4) {
+            float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
+            xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
+            xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+        }
+    }
+    const int n = r1 - r0;
+    for (int cb = 0; cb < n; cb += RPC) {
+        const int ce = min(n, cb + RPC);
+        const uint8_t* st = cs.wait(c, 1);
+        int i = cb + ((cs.warp - cb) % NCW + NCW) % NCW;
+        for (; i < ce; i += NCW) {
+            const uint4* row = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < UPL; ++j) WT::dot(row[cs.lane + 32 * j], xr + j * WT::EPU, a0, a1);
+            const float dot = warp_sum(a0 + a1);
+            if (cs.lane == 0) out(r0 + i, dot);
+        }
+        cs.release();
+    }
+}
+
+// gate/up pair phase: out(i, gate_dot, up_dot).
+template <class WT, class Out>
+__device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Out out) {
+    constexpr int K = HIDDEN;
+    constexpr int ESZ = Bytes<WT>::ESZ;
+    constexpr int RB = K * ESZ;
+    constexpr int UPL = K / (WT::EPU * 32);
+    constexpr int RPC = STAGE_BYTES / (2 * RB);
+    float xr[UPL * WT::EPU];
+#pragma unroll
+    for (int j = 0; j < UPL; ++j) {
+        const int e0 = (cs.lane + 32 * j) * WT::EPU;
+#pragma unroll
+        for (int e = 0; e < WT::EPU; e += 4) {
+            float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
+            xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
+            xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+        }
+    }
+    const int n = r1 - r0;
+    for (int cb = 0; cb < n; cb += RPC) {
+        const int ce = min(n, cb + RPC);
+        const int nin = ce - cb;
+        const uint8_t* st = cs.wait(c, 2);
+        int i = cb + ((cs.warp - cb) % NCW + NCW) % NCW;
+        for (; i < ce; i += NCW) {
+            const uint4* grow = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
+            const uint4* urow = reinterpret_cast<const uint4*>(st + (size_t)(nin + i - cb) * RB);
+            float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < UPL; ++j) {
+                WT::dot(grow[cs.lane + 32 * j], xr + j * WT::EPU, g0, g1);
+                WT::dot(urow[cs.lane + 32 * j], xr + j * WT::EPU, u0, u1);
+            }
+            const float gd = warp_sum(g0 + g1);
+            const float ud = warp_sum(u0 + u1);
+            if (cs.lane == 0) out(r0 + i, gd, ud);
+        }
+        cs.release();
+    }
+}
+
+// RMSNorm of src[1024] (fp32, smem) with bf16 weight -> dst (smem), over the
+// consumer threads: x * rsqrt(mean(x^2) + eps) * w  (int8_decoder.py:228-232).
+__device__ __forceinline__ void rmsnorm_1024(Cons& cs, const float* src, const __nv_bfloat16* w, float* dst) {
+    float ss = 0.f;
+    for (int i = cs.tid; i < HIDDEN; i += NCT) ss += src[i] * src[i];
+    ss = warp_sum(ss);
+    if (cs.lane == 0) cs.sm->red[cs.warp] = ss;
+    consumers_sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) tot += cs.sm->red[i];
+    const float rstd = rsqrtf(tot / (float)HIDDEN + RMS_EPS);
+    for (int i = cs.tid; i < HIDDEN; i += NCT) dst[i] = src[i] * rstd * __bfloat162float(w[i]);
+    consumers_sync();
+}
+
+__device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layer, int e) {
+    return epoch + 1u + (uint32_t)layer * TAGS_PER_LAYER + (uint32_t)e;
+}
+enum { E_H = 0, E_QKV = 1, E_PART = 2, E_ATTN = 3, E_ACT = 4, E_MLP = 5 };
+
+
+// ---------------------------------------------------------------------------
+// Attention for one (KV head g, position split s) item.
+// ---------------------------------------------------------------------------
+// Scores, online-softmax update and V accumulation for n positions whose K rows
+// start at kb and V rows at vb (bf16, HD elements per row, shared memory).
+// Thread t < 256 owns acc for q head (t >> 7) of the pair, dim (t & 127).
+__device__ __forceinline__ void attn_block(Cons& cs, const uint16_t* kb, const uint16_t* vb, int n,
+                                           float scale, float& acc) {
+    Smem* sm = cs.sm;
+    for (int p = cs.warp; p < n; p += NCW) {
+        const uint2 kw = *reinterpret_cast<const uint2*>(kb + p * HD + 4 * cs.lane);
+        const float k0 = bf16_bits_to_f32(kw.x & 0xffffu), k1 = bf16_bits_to_f32(kw.x >> 16);
+        const float k2 = bf16_bits_to_f32(kw.y & 0xffffu), k3 = bf16_bits_to_f32(kw.y >> 16);
+        const float* q0 = sm->q[0] + 4 * cs.lane;
+        const float* q1 = sm->q[1] + 4 * cs.lane;
+        float d0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
+        float d1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
+        d0 = warp_sum(d0);
+        d1 = warp_sum(d1);
+        if (cs.lane == 0) { sm->sc[0][p] = d0 * scale; sm->sc[1][p] = d1 * scale; }
+    }
+    consumers_sync();
+    if (cs.warp < 2) {
+        const int h = cs.warp;
+        const float sv = cs.lane < n ? sm->sc[h][cs.lane] : -INFINITY;
+        const float m_old = sm->m[h];
+        const float m_new = fmaxf(m_old, warp_max(sv));
+        const float pe = cs.lane < n ? expf(sv - m_new) : 0.f;
+        const float sum = warp_sum(pe);
+        sm->pe[h][cs.lane] = pe;
+        __syncwarp();
+        if (cs.lane == 0) {
+            const float corr = expf(m_old - m_new);
+            sm->l[h] = sm->l[h] * corr + sum;
+            sm->m[h] = m_new;
+            sm->corr[h] = corr;
+        }
+    }
+    consumers_sync();
+    if (cs.tid < 2 * HD) {
+        const int h = cs.tid >> 7, d = cs.tid & (HD - 1);
+        float a = acc * sm->corr[h];
+        for (int p = 0; p < n; ++p) a = fmaf(sm->pe[h][p], bf16_bits_to_f32(vb[p * HD + d]), a);
+        acc = a;
+    }
+    consumers_sync();
+}
+
+// QK RMSNorm over one 128-wide head then split-half RoPE at `pos`
+// (a10_int8_decode_kernel.cu:160-192, int8_decoder.py:234-240).  Lane holds
+// dims lane + 32j, so the RoPE partners (i, i+64) are j and j+2 of one lane.
+__device__ __forceinline__ void qk_norm_rope(const float* raw, const __nv_bfloat16* nw,
+                                             const __nv_bfloat16* cosr, const __nv_bfloat16* sinr,
+                                             int lane, float out[4]) {
+    float v[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { v[j] = raw[lane + 32 * j]; ss += v[j] * v[j]; }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)HD + RMS_EPS);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * __bfloat162float(nw[lane + 32 * j]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int i = lane + 32 * j;
+        out[j] = v[j] * __bfloat162float(cosr[i]) - v[j + 2] * __bfloat162float(sinr[i]);
+        out[j + 2] = v[j] * __bfloat162float(sinr[i + 64]) + v[j + 2] * __bfloat162float(cosr[i + 64]);
+    }
+}
+
+__device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo& G, int l,
+                               const LayerWeights& w, uint32_t epoch) {
+    Smem* sm = cs.sm;
+    const int par = l & 1;
+    const uint32_t tq = tag_of(epoch, l, E_QKV);
+    // raw q (two heads), k, v of KV head g
+    for (int i = cs.tid; i < 4 * HD; i += NCT) {
+        int src;
+        if (i < 2 * HD) src = 2 * G.g * HD + i;
+        else if (i < 3 * HD) src = QSZ + G.g * HD + (i - 2 * HD);
+        else src = QSZ + KVSZ + G.g * HD + (i - 3 * HD);
+        sm->raw[i] = __uint_as_float(poll_word(c, &c.ws->xqkv[par][src], tq, 10));
+    }
+    if (cs.tid < 2) { sm->m[cs.tid] = -INFINITY; sm->l[cs.tid] = 0.f; }
+    consumers_sync();
+    const int pos = G.c - 1;
+    const __nv_bfloat16* cosr = P.cos_t + (size_t)pos * HD;
+    const __nv_bfloat16* sinr = P.sin_t + (size_t)pos * HD;
+    if (cs.warp < 2) {
+        float o[4];
+        qk_norm_rope(sm->raw + cs.warp * HD, (const __nv_bfloat16*)w.q_norm_weight, cosr, sinr, cs.lane, o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm->q[cs.warp][cs.lane + 32 * j] = o[j];
+    } else if (cs.warp == 2 && G.owner) {
+        float o[4];
+        qk_norm_rope(sm->raw + 2 * HD, (const __nv_bfloat16*)w.k_norm_weight, cosr, sinr, cs.lane, o);
+        const size_t off = (((size_t)l * NKVH + G.g) * (size_t)P.max_seq + pos) * HD;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = cs.lane + 32 * j;
+            const uint16_t kb = (uint16_t)f32_to_bf16_bits(o[j]);
+            const uint16_t vb = (uint16_t)f32_to_bf16_bits(sm->raw[3 * HD + i]);
+            sm->kvcur[0][i] = kb;
+            sm->kvcur[1][i] = vb;
+            reinterpret_cast<uint16_t*>(P.kc)[off + i] = kb;
+            reinterpret_cast<uint16_t*>(P.vc)[off + i] = vb;
+        }
+    }
+    consumers_sync();
+    float acc = 0.f;
+    for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS) {
+        const int n = min(KV_CHUNK_POS, G.past1 - p);
+        const uint8_t* st = cs.wait(c, 3);
+        attn_block(cs, reinterpret_cast<const uint16_t*>(st),
+                   reinterpret_cast<const uint16_t*>(st + KV_CHUNK_POS * HD * 2), n, P.attn_scale, acc);
+        cs.release();
+    }
+    if (G.owner) attn_block(cs, sm->kvcur[0], sm->kvcur[1], 1, P.attn_scale, acc);
+    if (G.S == 1) {
+        if (cs.tid < 2 * HD) {
+            const float o = acc / sm->l[cs.tid >> 7];
+            st_tagged(&c.ws->xattn[par][G.g * 2 * HD + cs.tid], tag_of(epoch, l, E_ATTN), __float_as_uint(o));
+        }
+        return;
+    }
+    // Split-K: publish (acc, m, l), then merge this split's slice of the pair's 256 outputs.
+    const uint32_t tp = tag_of(epoch, l, E_PART);
+    uint64_t* part = c.ws->xpart[par];
+    if (cs.tid < 2 * HD) st_tagged(&part[G.item * PART_WORDS + cs.tid], tp, __float_as_uint(acc));
+    if (cs.tid < 2) {
+        st_tagged(&part[G.item * PART_WORDS + 2 * HD + cs.tid], tp, __float_as_uint(sm->m[cs.tid]));
+        st_tagged(&part[G.item * PART_WORDS + 2 * HD + 2 + cs.tid], tp, __float_as_uint(sm->l[cs.tid]));
+    }
+    const int j0 = split_lo(2 * HD, G.S, G.s), j1 = split_lo(2 * HD, G.S, G.s + 1);
+    const int j = j0 + cs.tid;
+    if (j < j1) {
+        const int h = j >> 7;
+        const int base_item = G.g * G.S;
+        float M = -INFINITY;
+        for (int t = 0; t < G.S; ++t)
+            M = fmaxf(M, __uint_as_float(poll_word(c, &part[(base_item + t) * PART_WORDS + 2 * HD + h], tp, 11)));
+        float L = 0.f, o = 0.f;
+        for (int t = 0; t < G.S; ++t) {
+            const uint64_t* pp = &part[(base_item + t) * PART_WORDS];
+            const float mt = __uint_as_float(poll_word(c, pp + 2 * HD + h, tp, 12));
+            const float lt = __uint_as_float(poll_word(c, pp + 2 * HD + 2 + h, tp, 12));
+            const float at = __uint_as_float(poll_word(c, pp + j, tp, 12));
+            const float e = expf(mt - M);
+            L = fmaf(lt, e, L);
+            o = fmaf(at, e, o);
+        }
+        st_tagged(&c.ws->xattn[par][G.g * 2 * HD + j], tag_of(epoch, l, E_ATTN), __float_as_uint(o / L));
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// Consumer main: the layer loop.
+// ---------------------------------------------------------------------------
+template <class WT>
+__device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint32_t epoch, int token,
+                              unsigned long long& cta_key) {
+    Smem* sm = c.sm;
+    Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
+    Workspace* ws = c.ws;
+    const bool cta0 = G.b == 0;
+    if (!*(volatile int*)&sm->abort_flag) {
+        const __nv_bfloat16* er = (const __nv_bfloat16*)P.embed + (size_t)token * HIDDEN;
+        for (int i = cs.tid; i < HIDDEN; i += NCT) sm->h[i] = __bfloat162float(er[i]);
+    }
+    for (int l = 0; l < P.L; ++l) {
+        const int par = l & 1;
+        const LayerWeights& w = P.layers[l];
+        if (consumers_sync_abort(c)) break;
+        if (l > 0) {
+            const uint32_t t = tag_of(epoch, l, E_H);
+            for (int i = cs.tid; i < HIDDEN; i += NCT) {
+                sm->h[i] = bf16_bits_to_f32(poll_word(c, &ws->xh[par][i], t, 20));
+                if (cta0 && P.layer_hidden) P.layer_hidden[(size_t)(l - 1) * HIDDEN + i] = sm->h[i];
+            }
+        }
+        rmsnorm_1024(cs, sm->h, (const __nv_bfloat16*)w.input_layernorm_weight, sm->x);
+        // --- QKV ---
+        {
+            const ScalePointers* sp = WT::HAS_SCALE ? &P.scales[l] : nullptr;
+            const uint32_t t = tag_of(epoch, l, E_QKV);
+            const bool skip = (l == 0 && G.b == P.skip_cta);
+            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, [&](int r, float d) {
+                if (WT::HAS_SCALE) {
+                    const float s = r < QSZ ? sp->q_scale[r] : (r < QSZ + KVSZ ? sp->k_scale[r - QSZ] : sp->v_scale[r - QSZ - KVSZ]);
+                    d *= s;
+                }
+                if (!skip) st_tagged(&ws->xqkv[par][r], t, __float_as_uint(d));
+            });
+        }
+        // --- attention (only CTAs that own an item) ---
+        if (G.item >= 0) {
+            if (consumers_sync_abort(c)) break;
+            attention_item(P, c, cs, G, l, w, epoch);
+        }
+        // --- O projection + residual ---
+        if (consumers_sync_abort(c)) break;
+        {
+            const uint32_t t = tag_of(epoch, l, E_ATTN);
+            for (int i = cs.tid; i < QSZ; i += NCT) sm->x[i] = __uint_as_float(poll_word(c, &ws->xattn[par][i], t, 30));
+        }
+        consumers_sync();
+        {
+            const float* so = WT::HAS_SCALE ? P.scales[l].o_scale : nullptr;
+            const uint32_t t = tag_of(epoch, l, E_ACT);
+            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, [&](int r, float d) {
+                if (WT::HAS_SCALE) d *= so[r];
+                st_tagged(&ws->xact[par][r], t, __float_as_uint(d + sm->h[r]));
+            });
+        }
+        // --- post-attention norm + gate/up ---
+        if (consumers_sync_abort(c)) break;
+        {
+            const uint32_t t = tag_of(epoch, l, E_ACT);
+            for (int i = cs.tid; i < HIDDEN; i += NCT) sm->act[i] = __uint_as_float(poll_word(c, &ws->xact[par][i], t, 40));
+        }
+        rmsnorm_1024(cs, sm->act, (const __nv_bfloat16*)w.post_attn_layernorm_weight, sm->x);
+        {
+            const float* sg = WT::HAS_SCALE ? P.scales[l].gate_scale : nullptr;
+            const float* su = WT::HAS_SCALE ? P.scales[l].up_scale : nullptr;
+            const uint32_t t = tag_of(epoch, l, E_MLP);
+            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, [&](int r, float gd, float ud) {
+                if (WT::HAS_SCALE) { gd *= sg[r]; ud *= su[r]; }
+                const float silu = gd / (1.0f + expf(-gd));
+                st_tagged(&ws->xmlp[par][r], t, __float_as_uint(silu * ud));
+            });
+        }
+        // --- down + residual -> next h (bf16) ---
+        if (consumers_sync_abort(c)) break;
+        {
+            const uint32_t t = tag_of(epoch, l, E_MLP);
+            for (int i = cs.tid; i < INTER; i += NCT) sm->x[i] = __uint_as_float(poll_word(c, &ws->xmlp[par][i], t, 50));
+        }
+        consumers_sync();
+        {
+            const float* sd = WT::HAS_SCALE ? P.scales[l].down_scale : nullptr;
+            const uint32_t t = tag_of(epoch, l + 1, E_H);
+            uint64_t* dst = ws->xh[(l + 1) & 1];
+            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, [&](int r, float d) {
+                if (WT::HAS_SCALE) d *= sd[r];
+                st_tagged(&dst[r], t, f32_to_bf16_bits(d + sm->act[r]));
+            });
+        }
+    }
+    // --- final norm + LM head + argmax ---
+    cta_key = 0ull;
+    if (consumers_sync_abort(c)) return;
+    {
+        const uint32_t t = tag_of(epoch, P.L, E_H);
+        for (int i = cs.tid; i < HIDDEN; i += NCT) {
+            sm->h[i] = bf16_bits_to_f32(poll_word(c, &ws->xh[P.L & 1][i], t, 60));
+            if (cta0 && P.layer_hidden) P.layer_hidden[(size_t)(P.L - 1) * HIDDEN + i] = sm->h[i];
+        }
+    }
+    rmsnorm_1024(cs, sm->h, (const __nv_bfloat16*)P.final_norm, sm->x);
+    if (cta0 && P.g_normalized)
+        for (int i = cs.tid; i < HIDDEN; i += NCT) P.g_normalized[i] = sm->x[i];
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+    {
+        const float* ls = P.lm_scale;
+        float* logits = P.logits;
+        mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, [&](int r, float d) {
+            if (WT::HAS_SCALE) d *= ls[r];
+            if (logits) logits[r] = d;
+            if (d > best_v) { best_v = d; best_i = r; }
+        });
+    }
+    if (cs.lane == 0) {
+        sm->best[cs.warp] = best_i == 0x7fffffff ? 0ull
+                           : (((unsigned long long)float_order_key(best_v)) << 32) | (uint32_t)(~(uint32_t)best_i);
+    }
+    consumers_sync();
+    if (cs.tid == 0) {
+        unsigned long long k = 0ull;
+        for (int i = 0; i < NCW; ++i) k = sm->best[i] > k ? sm->best[i] : k;
+        cta_key = k;
+    }
+}
+
+template <class WT>
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams P) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem* sm = reinterpret_cast<Smem*>(smem_raw);
+    Ctx c{sm, P.ws, P.budget_ns};
+    Geo G;
+    G.init(P);
+    const uint32_t epoch = ld_relaxed32(&P.ws->epoch);
+    int token = P.token_in_dev ? *(volatile const int*)P.token_in_dev : P.token_in;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&sm->full[s], 1);
+            mbar_init(&sm->empty[s], NCW);
+        }
+        sm->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (token < 0 || token >= VOCAB) {
+        if (threadIdx.x == 0) {
+            if (G.b == 0) record_error(c, MQ_DEV_BAD_TOKEN, token);
+            sm->abort_flag = 1;
+        }
+        token = 0;
+    }
+    __syncthreads();
+    unsigned long long cta_key = 0ull;
+    if (threadIdx.x >= NCT) {
+        if (threadIdx.x == NCT) producer_main<WT>(P, c, G);
+    } else {
+        consumer_main<WT>(P, c, G, epoch, token, cta_key);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Workspace* ws = P.ws;
+        if (!sm->abort_flag && cta_key) atomicMax(&ws->argmax, cta_key);
+        __threadfence();
+        const unsigned old = atomicAdd(&ws->exit_ctr, 1u);
+        if (old == gridDim.x - 1) {
+            __threadfence();
+            const unsigned long long key = atomicExch(&ws->argmax, 0ull);
+            const int err = atomicAdd(&ws->err_code, 0);
+            *P.token_out = (err != 0 || key == 0ull) ? -1 : (int)(~(uint32_t)key);
+            atomicExch(&ws->exit_ctr, 0u);
+            atomicExch(&ws->epoch, epoch + (uint32_t)(P.L + 1) * TAGS_PER_LAYER);
+            __threadfence();
+        }
+    }
+}
+
+// Standalone streaming matvec with the same ring and dot code (mq_matvec).
+struct MatvecParams {
+    const void* W;
+    const float* scale;
+    const float* x;
+    float* y;
+    Workspace* ws;
+    unsigned long long budget_ns;
+    int M;
+};
+
+template <class WT, int K>
+__global__ void __launch_bounds__(NTHREADS, 1) matvec_kernel(const MatvecParams P) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem* sm = reinterpret_cast<Smem*>(smem_raw);
+    Ctx c{sm, P.ws, P.budget_ns};
+    const int r0 = split_lo(P.M, gridDim.x, blockIdx.x), r1 = split_lo(P.M, gridDim.x, blockIdx.x + 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; ++s) { mbar_init(&sm->full[s], 1); mbar_init(&sm->empty[s], NCW); }
+        sm->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < K; i += NTHREADS) sm->x[i] = P.x[i];
+    __syncthreads();
+    if (threadIdx.x >= NCT) {
+        if (threadIdx.x == NCT) {
+            Producer pr{sm, 0};
+            pr.rows(c, (const uint8_t*)P.W, r0, r1, K * Bytes<WT>::ESZ);
+            const uint32_t first = pr.seq > (uint32_t)NSTAGE ? pr.seq - NSTAGE : 0u;
+            for (uint32_t q = first; q < pr.seq; ++q) {
+                unsigned long long t0 = globaltimer();
+                while (!mbar_test(&sm->full[q % NSTAGE], (q / NSTAGE) & 1))
+                    if (globaltimer() - t0 > c.budget) break;
+            }
+        }
+    } else {
+        Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
+        const float* sc = P.scale;
+        float* y = P.y;
+        mv_phase<WT, K>(c, cs, r0, r1, sm->x, [&](int r, float d) {
+            if (WT::HAS_SCALE) d *= sc[r];
+            y[r] = d;
+        });
+    }
+    __syncthreads();
+}
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+
+constexpr int MAX_DEV = 64;
+struct DevState {
+    Workspace* ws = nullptr;
+    int num_sms = 0;
+    bool attr_set[4] = {false, false, false, false};
+    unsigned long long launches = 0;
+};
+DevState g_dev[MAX_DEV];
+unsigned long long g_budget_ns = 2000000000ull;
+int g_skip_cta = -1;
+int g_pos_per_split = 256;
+
+int dev_state(DevState** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= MAX_DEV) return MQ_ERR_DEVICE;
+    DevState& d = g_dev[dev];
+    if (!d.ws) {
+        int sms = 0;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return (int)e;
+        if (sms < NKVH) return MQ_ERR_DEVICE;
+        Workspace* ws = nullptr;
+        if ((e = cudaMalloc(&ws, sizeof(Workspace))) != cudaSuccess) return (int)e;
+        if ((e = cudaMemset(ws, 0, sizeof(Workspace))) != cudaSuccess) return (int)e;
+        if ((e = cudaDeviceSynchronize()) != cudaSuccess) return (int)e;
+        d.ws = ws;
+        d.num_sms = sms;
+        if (const char* env = getenv("MQ_POS_PER_SPLIT")) {
+            int v = atoi(env);
+            if (v > 0) g_pos_per_split = v;
+        }
+    }
+    *out = &d;
+    return 0;
+}
+
+template <class K>
+int ensure_smem_attr(DevState& d, int slot, K kernel) {
+    if (d.attr_set[slot]) return 0;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    if (e != cudaSuccess) return (int)e;
+    d.attr_set[slot] = true;
+    return 0;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int choose_splits(int cache_len, int nb) {
+    int s = (cache_len + g_pos_per_split - 1) / g_pos_per_split;
+    s = s < 1 ? 1 : s;
+    s = s > MAX_SPLITS ? MAX_SPLITS : s;
+    while (NKVH * s > nb) --s;
+    if (s > cache_len) s = cache_len;
+    return s < 1 ? 1 : s;
+}
+
+int launch_step(int kind, DecodeParams& P, cudaStream_t stream) {
+    DevState* d = nullptr;
+    int rc = dev_state(&d);
+    if (rc) return rc;
+    P.ws = d->ws;
+    P.budget_ns = g_budget_ns;
+    P.skip_cta = g_skip_cta;
+    g_skip_cta = -1;
+    P.splits = choose_splits(P.position + 1, d->num_sms);
+    // Tags are 32-bit epochs; clear the hand-off buffers long before they wrap.
+    const unsigned long long per_launch = (unsigned long long)(P.L + 1) * TAGS_PER_LAYER;
+    if ((d->launches + 1) * per_launch > 0xF0000000ull) {
+        cudaError_t e = cudaMemsetAsync(d->ws, 0, sizeof(Workspace), stream);
+        if (e != cudaSuccess) return (int)e;
+        d->launches = 0;
+    }
+    d->launches++;
+    void* args[] = {&P};
+    cudaError_t e;
+    if (kind == 0) {
+        if ((rc = ensure_smem_attr(*d, 0, decode_kernel<W8>))) return rc;
+        e = cudaLaunchCooperativeKernel((const void*)decode_kernel<W8>, dim3(d->num_sms), dim3(NTHREADS), args,
+                                        sizeof(Smem), stream);
+    } else {
+        if ((rc = ensure_smem_attr(*d, 1, decode_kernel<W16>))) return rc;
+        e = cudaLaunchCooperativeKernel((const void*)decode_kernel<W16>, dim3(d->num_sms), dim3(NTHREADS), args,
+                                        sizeof(Smem), stream);
+    }
+    return (int)e;
+}
+
+int check_common(const void* embed, const LayerWeights* lw, const void* fnorm, const void* lm, const void* cos_t,
+                 const void* sin_t, void* kc, void* vc, int L, int position, int max_seq) {
+    if (!embed || !lw || !fnorm || !lm || !cos_t || !sin_t || !kc || !vc) return MQ_ERR_ARG;
+    if (!aligned16(lm) || !aligned16(kc) || !aligned16(vc) || !aligned16(embed)) return MQ_ERR_ARG;
+    if (L <= 0 || max_seq <= 0) return MQ_ERR_ARG;
+    if (position < 0 || position >= max_seq) return MQ_ERR_POSITION;
+    return 0;
+}
+
+}  // namespace
+}  // namespace mq
+
+using namespace mq;
+
+extern "C" int launch_a10_int8_decode(
+    int input_token_id, int* output_token_id, const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale, const void* cos_table,
+    const void* sin_table, void* k_cache, void* v_cache, void* /*hidden_buffer*/, void* /*g_activations*/,
+    void* /*g_residual*/, void* /*g_q*/, void* /*g_k*/, void* /*g_v*/, void* /*g_attn_out*/,
+    void* /*g_mlp_intermediate*/, void* g_normalized, void* /*block_max_vals*/, void* /*block_max_idxs*/,
+    int num_layers, int position, int cache_len, int max_seq_len, float attn_scale, const ScalePointers* scales,
+    cudaStream_t stream) {
+    int rc = check_common(embed_weight, layer_weights, final_norm_weight, lm_head_weight, cos_table, sin_table,
+                          k_cache, v_cache, num_layers, position, max_seq_len);
+    if (rc) return rc;
+    if (!output_token_id || !lm_head_scale || !scales) return MQ_ERR_ARG;
+    if (cache_len != position + 1) return MQ_ERR_POSITION;
+    if (input_token_id < 0 || input_token_id >= VOCAB) return MQ_ERR_TOKEN;
+    DecodeParams P{};
+    P.embed = embed_weight; P.layers = layer_weights; P.scales = scales; P.final_norm = final_norm_weight;
+    P.lm_w = lm_head_weight; P.lm_scale = lm_head_scale;
+    P.cos_t = (const __nv_bfloat16*)cos_table; P.sin_t = (const __nv_bfloat16*)sin_table;
+    P.kc = (__nv_bfloat16*)k_cache; P.vc = (__nv_bfloat16*)v_cache;
+    P.g_normalized = (float*)g_normalized; P.token_out = output_token_id;
+    P.token_in = input_token_id; P.L = num_layers; P.position = position; P.max_seq = max_seq_len;
+    P.attn_scale = attn_scale;
+    return launch_step(0, P, stream);
+}
+
+extern "C" int launch_a10_decode(
+    int input_token_id, int* output_token_id, const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const void* cos_table, const void* sin_table,
+    void* k_cache, void* v_cache, void* /*hidden_buffer*/, void* /*g_activations*/, void* /*g_residual*/,
+    void* /*g_q*/, void* /*g_k*/, void* /*g_v*/, void* /*g_attn_out*/, void* /*g_mlp_intermediate*/,
+    void* g_normalized, void* /*block_max_vals*/, void* /*block_max_idxs*/, int num_layers, int position,
+    int cache_len, int max_seq_len, float attn_scale, cudaStream_t stream) {
+    int rc = check_common(embed_weight, layer_weights, final_norm_weight, lm_head_weight, cos_table, sin_table,
+                          k_cache, v_cache, num_layers, position, max_seq_len);
+    if (rc) return rc;
+    if (!output_token_id) return MQ_ERR_ARG;
+    if (cache_len != position + 1) return MQ_ERR_POSITION;
+    if (input_token_id < 0 || input_token_id >= VOCAB) return MQ_ERR_TOKEN;
+    DecodeParams P{};
+    P.embed = embed_weight; P.layers = layer_weights; P.final_norm = final_norm_weight; P.lm_w = lm_head_weight;
+    P.cos_t = (const __nv_bfloat16*)cos_table; P.sin_t = (const __nv_bfloat16*)sin_table;
+    P.kc = (__nv_bfloat16*)k_cache; P.vc = (__nv_bfloat16*)v_cache;
+    P.g_normalized = (float*)g_normalized; P.token_out = output_token_id;
+    P.token_in = input_token_id; P.L = num_layers; P.position = position; P.max_seq = max_seq_len;
+    P.attn_scale = attn_scale;
+    return launch_step(1, P, stream);
+}
+
+extern "C" int mq_decode_multi(int weight_kind, const int* d_token_in, int* d_tokens_out, int num_steps,
+                               const void* embed_weight, const LayerWeights* layer_weights,
+                               const void* final_norm_weight, const void* lm_head_weight,
+                               const float* lm_head_scale, const ScalePointers* scales, const void* cos_table,
+                               const void* sin_table, void* k_cache, void* v_cache, float* g_normalized,
+                               float* d_logits, float* d_layer_hidden, int num_layers, int position,
+                               int max_seq_len, float attn_scale, cudaStream_t stream) {
+    if (weight_kind != 0 && weight_kind != 1) return MQ_ERR_ARG;
+    if (!d_token_in || !d_tokens_out || num_steps <= 0) return MQ_ERR_ARG;
+    int rc = check_common(embed_weight, layer_weights, final_norm_weight, lm_head_weight, cos_table, sin_table,
+                          k_cache, v_cache, num_layers, position, max_seq_len);
+    if (rc) return rc;
+    if (position + num_steps > max_seq_len) return MQ_ERR_POSITION;
+    if (weight_kind == 0 && (!lm_head_scale || !scales)) return MQ_ERR_ARG;
+    for (int j = 0; j < num_steps; ++j) {
+        DecodeParams P{};
+        P.embed = embed_weight; P.layers = layer_weights; P.scales = scales; P.final_norm = final_norm_weight;
+        P.lm_w = lm_head_weight; P.lm_scale = lm_head_scale;
+        P.cos_t = (const __nv_bfloat16*)cos_table; P.sin_t = (const __nv_bfloat16*)sin_table;
+        P.kc = (__nv_bfloat16*)k_cache; P.vc = (__nv_bfloat16*)v_cache;
+        const bool last = j == num_steps - 1;
+        P.g_normalized = last ? g_normalized : nullptr;
+        P.logits = last ? d_logits : nullptr;
+        P.layer_hidden = last ? d_layer_hidden : nullptr;
+        P.token_in_dev = j == 0 ? d_token_in : d_tokens_out + (j - 1);
+        P.token_out = d_tokens_out + j;
+        P.L = num_layers; P.position = position + j; P.max_seq = max_seq_len; P.attn_scale = attn_scale;
+        if ((rc = launch_step(weight_kind, P, stream))) return rc;
+    }
+    return 0;
+}
+
+extern "C" int mq_matvec(int weight_kind, const void* W, const float* scale, const float* x, float* y, int M, int K,
+                         cudaStream_t stream) {
+    if (!W || !x || !y || M <= 0) return MQ_ERR_ARG;
+    if (weight_kind == 0 && !scale) return MQ_ERR_ARG;
+    if (weight_kind != 0 && weight_kind != 1) return MQ_ERR_ARG;
+    if (!aligned16(W) || !aligned16(x)) return MQ_ERR_ARG;
+    if (K != 1024 && K != 2048 && K != 3072) return MQ_ERR_SIZE;
+    DevState* d = nullptr;
+    int rc = dev_state(&d);
+    if (rc) return rc;
+    MatvecParams P{W, scale, x, y, d->ws, g_budget_ns, M};
+    void* args[] = {&P};
+    const void* fn = nullptr;
+#define MQ_MV_CASE(WT, KK)                                                                   \
+    {                                                                                        \
+        cudaError_t e = cudaFuncSetAttribute(matvec_kernel<WT, KK>,                          \
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                             (int)sizeof(Smem));                             \
+        if (e != cudaSuccess) return (int)e;                                                 \
+        fn = (const void*)matvec_kernel<WT, KK>;                                             \
+    }
+    if (weight_kind == 0) {
+        if (K == 1024) MQ_MV_CASE(W8, 1024) else if (K == 2048) MQ_MV_CASE(W8, 2048) else MQ_MV_CASE(W8, 3072)
+    } else {
+        if (K == 1024) MQ_MV_CASE(W16, 1024) else if (K == 2048) MQ_MV_CASE(W16, 2048) else MQ_MV_CASE(W16, 3072)
+    }
+#undef MQ_MV_CASE
+    return (int)cudaLaunchKernel(fn, dim3(d->num_sms), dim3(NTHREADS), args, sizeof(Smem), stream);
+}
+
+extern "C" int mq_device_status(int* code, int* info, int clear) {
+    DevState* d = nullptr;
+    int rc = dev_state(&d);
+    if (rc) return rc;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return (int)e;
+    int h[2] = {0, 0};
+    e = cudaMemcpy(h, &d->ws->err_code, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return (int)e;
+    if (code) *code = h[0];
+    if (info) *info = h[1];
+    if (clear) {
+        e = cudaMemset(&d->ws->err_code, 0, sizeof(h));
+        if (e != cudaSuccess) return (int)e;
+        e = cudaDeviceSynchronize();
+    }
+    return (int)e;
+}
+
+extern "C" int mq_set_wait_budget_ns(uint64_t ns) {
+    if (ns == 0) return MQ_ERR_ARG;
+    g_budget_ns = ns;
+    return 0;
+}
+
+extern "C" int mq_inject_skip_publish(int enable, int cta) {
+    g_skip_cta = enable ? cta : -1;
+    return 0;
+}
+
+extern "C" int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads) {
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_ctas) *num_ctas = e == cudaSuccess ? sms : 0;
+    if (smem_bytes) *smem_bytes = (int)sizeof(Smem);
+    if (threads) *threads = NTHREADS;
+    return (int)e;
+}

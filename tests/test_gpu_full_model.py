@@ -22,10 +22,8 @@ def test_full_model_200_steps():
     inputs = [start] + toks[:-1]
     agree = 0
     for i, t_in in enumerate(inputs):
-        t_o = orc.decode_step(t_in)
-        agree += int(t_o == toks[i])
+        agree += int(orc.decode_step(t_in) == toks[i])
     assert agree >= 0.95 * steps, f"{agree}/{steps}"
-    # logits of one more step on both sides
     lg = torch.empty(mq.CFG.vocab_size, dtype=torch.float32, device="cuda")
     dec.decode_steps(toks[-1], 1, logits=lg)
     _, l_o, _ = orc.step(toks[-1], want_logits=True)

@@ -27,7 +27,14 @@ def close(a, b, rel=REL, cos=COS):
 
 @pytest.fixture(scope="module")
 def small_state():
-    return mq.make_synthetic_state(seed=0, num_layers=2)
+    """2-layer synthetic model with non-unit norm weights, so every norm weight
+    (input, post-attention, q_norm, k_norm, final) is exercised."""
+    st = mq.make_synthetic_state(seed=0, num_layers=2)
+    g = torch.Generator().manual_seed(99)
+    for k in st:
+        if "norm" in k:
+            st[k] = (1.0 + 0.2 * torch.randn(st[k].shape, generator=g)).to(torch.bfloat16)
+    return st
 
 
 def build_int8(state, L, max_seq):

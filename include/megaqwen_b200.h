@@ -161,6 +161,15 @@ int mq_set_wait_budget_ns(uint64_t ns);
  * bounded wait and reports MQ_DEV_TIMEOUT_EXCHANGE.  Cleared after one launch. */
 int mq_inject_skip_publish(int enable, int cta);
 
+/* Tracing: when dev_buf is non-NULL, every later decode launch writes
+ * %globaltimer stamps (ns) into dev_buf[cta * slots_per_cta + slot], slot =
+ * layer * 10 + event (events: 0 layer input ready, 1 QKV published, 2 attention
+ * published, 3 attention gathered, 4 O published, 5 post-norm done, 6 gate/up
+ * published, 7 MLP gathered, 8 down published; slots num_layers*10 + 0/1: final
+ * hidden gathered / LM head done).  NULL disables.  No reference counterpart
+ * (the reference has no tracing). */
+int mq_set_trace(unsigned long long* dev_buf, int slots_per_cta);
+
 /* Number of CTAs (one per SM) and dynamic shared memory the decode kernel uses. */
 int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads);
 

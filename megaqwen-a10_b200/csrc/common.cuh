@@ -31,6 +31,14 @@ constexpr int STAGE_BYTES = 16384;
 constexpr int NSTAGE = 11;
 constexpr int KV_CHUNK_POS = STAGE_BYTES / (2 * HD * 2);  // 32 positions of K then V
 constexpr int MAX_SPLITS = 18;                // attention splits per KV head
+constexpr int MAX_LAYERS = 32;                // pointer/scale tables staged in shared memory
+constexpr int MIN_CTAS = 148;                 // row shares below assume >= 148 CTAs (B200)
+constexpr int QKV_MAXR = (QKV_ROWS + MIN_CTAS - 1) / MIN_CTAS;   // 28 rows per CTA
+constexpr int O_MAXR = (HIDDEN + MIN_CTAS - 1) / MIN_CTAS;       // 7
+constexpr int GU_MAXR = (INTER + MIN_CTAS - 1) / MIN_CTAS;       // 21
+constexpr int LM_MAXR = (VOCAB + MIN_CTAS - 1) / MIN_CTAS;       // 1027
+constexpr int SCL_O = QKV_MAXR, SCL_G = SCL_O + O_MAXR, SCL_U = SCL_G + GU_MAXR, SCL_D = SCL_U + GU_MAXR;
+constexpr int SCL_STRIDE = SCL_D + O_MAXR;                       // 84 scales per layer per CTA
 
 // ---------------------------------------------------------------------------
 // Tagged hand-off words.  A value crossing CTAs is published as one 64-bit

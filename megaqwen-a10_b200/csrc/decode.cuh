@@ -49,7 +49,13 @@ struct DecodeParams {
     int splits;                     // attention splits per KV head
     float attn_scale;
     int skip_cta;                   // test hook: CTA that skips its layer-0 QKV publish (-1: none)
+    unsigned long long* trace;      // optional [gridDim.x][trace_slots] globaltimer stamps
+    int trace_slots;
 };
+
+// Trace slots: per layer l, stamps at l * TRACE_PER_LAYER + event.
+enum { TR_START = 0, TR_QKV = 1, TR_ATTN = 2, TR_OIN = 3, TR_O = 4, TR_NORM2 = 5, TR_GU = 6, TR_MLPIN = 7,
+       TR_DOWN = 8, TRACE_PER_LAYER = 10 };
 
 // Shared-memory layout (dynamic).
 struct Smem {
@@ -67,6 +73,10 @@ struct Smem {
     float pe[2][KV_CHUNK_POS];
     uint16_t kvcur[2][HD];   // current-position K and V, bf16
     unsigned long long best[NCW];
+    const void* lw[MAX_LAYERS][11];      // LayerWeights of every layer
+    const float* ls[MAX_LAYERS][7];      // ScalePointers of every layer
+    float scl[MAX_LAYERS * SCL_STRIDE];  // this CTA's per-row scales of every layer
+    float lm_scl[LM_MAXR + 1];           // this CTA's LM-head row scales
     int abort_flag;
 };
 

@@ -21,6 +21,27 @@
 #include "decode.cuh"
 #include <stdlib.h>
 
+// MQ_DEBUG_STAMPS (development aid, off by default): consumer thread 0 of CTA 1
+// appends (id, clock64) pairs to a buffer set with mqdbg_set_stamp_buffer.
+#ifndef MQ_DEBUG_STAMPS
+#define MQ_DEBUG_STAMPS 0
+#endif
+namespace mq {
+__device__ int g_dbg_n;
+__device__ unsigned long long* g_dbg_buf;
+__device__ __forceinline__ void dbg(int id) {
+#if MQ_DEBUG_STAMPS
+    if (blockIdx.x == 1 && threadIdx.x == 0 && g_dbg_buf && g_dbg_n < 4000) {
+        g_dbg_buf[2 * g_dbg_n] = id;
+        g_dbg_buf[2 * g_dbg_n + 1] = clock64();
+        ++g_dbg_n;
+    }
+#else
+    (void)id;
+#endif
+}
+}  // namespace mq
+
 namespace mq {
 
 struct Ctx {
@@ -92,7 +113,7 @@ __device__ __forceinline__ bool consumers_sync_abort(Ctx& c) {
         : "memory");
     return any != 0;
 }
-__device__ __forceinline__ void consumers_sync() { named_bar(1, NCT); }
+__device__ __forceinline__ void consumers_sync() { dbg(600); named_bar(1, NCT); dbg(700); }
 
 // ---------------------------------------------------------------------------
 // Work geometry, shared by producer and consumers so both walk the same chunks.
@@ -248,7 +269,9 @@ struct Cons {
 
     __device__ const uint8_t* wait(Ctx& c, int where) {
         const uint32_t stage = seq % NSTAGE;
+        dbg(100 + where);
         mbar_wait(c, &sm->full[stage], (seq / NSTAGE) & 1, where);
+        dbg(200 + where);
         return sm->ring[stage];
     }
     __device__ void release() {
@@ -261,8 +284,8 @@ struct Cons {
 // Matvec over rows [r0, r1) of one projection streamed through the ring.
 // Row i (phase-relative) is handled by warp i % NCW; lane holds the activation
 // elements of its fixed 16-byte units in registers for the whole phase.
-template <class WT, int K, class Out>
-__device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Out out) {
+template <class WT, int K, class Scl, class Out>
+__device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
@@ -284,12 +307,14 @@ __device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const
         const uint8_t* st = cs.wait(c, 1);
         int i = cb + ((cs.warp - cb) % NCW + NCW) % NCW;
         for (; i < ce; i += NCW) {
+            const float sc = scl(r0 + i);
             const uint4* row = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int j = 0; j < UPL; ++j) WT::dot(row[cs.lane + 32 * j], xr + j * WT::EPU, a0, a1);
             const float dot = warp_sum(a0 + a1);
-            if (cs.lane == 0) out(r0 + i, dot);
+            if (cs.lane == 0) out(r0 + i, dot * sc);
+            dbg(300);
         }
         cs.release();
     }
@@ -297,7 +322,8 @@ __device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const
 
 // gate/up pair phase: out(i, gate_dot, up_dot).
 template <class WT, class Out>
-__device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Out out) {
+__device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const float* sg,
+                                         const float* su, Out out) {
     constexpr int K = HIDDEN;
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
@@ -321,6 +347,8 @@ __device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const
         const uint8_t* st = cs.wait(c, 2);
         int i = cb + ((cs.warp - cb) % NCW + NCW) % NCW;
         for (; i < ce; i += NCW) {
+            float gsc = 1.f, usc = 1.f;
+            if (WT::HAS_SCALE) { gsc = sg[i]; usc = su[i]; }  // phase-relative, shared memory
             const uint4* grow = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
             const uint4* urow = reinterpret_cast<const uint4*>(st + (size_t)(nin + i - cb) * RB);
             float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
@@ -331,17 +359,35 @@ __device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const
             }
             const float gd = warp_sum(g0 + g1);
             const float ud = warp_sum(u0 + u1);
-            if (cs.lane == 0) out(r0 + i, gd, ud);
+            if (cs.lane == 0) out(r0 + i, gd * gsc, ud * usc);
         }
         cs.release();
     }
 }
 
-// RMSNorm of src[1024] (fp32, smem) with bf16 weight -> dst (smem), over the
-// consumer threads: x * rsqrt(mean(x^2) + eps) * w  (int8_decoder.py:228-232).
-__device__ __forceinline__ void rmsnorm_1024(Cons& cs, const float* src, const __nv_bfloat16* w, float* dst) {
+constexpr int NORM_PER = (HIDDEN + NCT - 1) / NCT;
+struct NormW {  // one thread's share of a 1024-wide bf16 norm weight, loaded ahead of use
+    float v[NORM_PER];
+    __device__ __forceinline__ void load(const Cons& cs, const void* w) {
+        const __nv_bfloat16* p = (const __nv_bfloat16*)w;
+#pragma unroll
+        for (int k = 0; k < NORM_PER; ++k) {
+            const int i = cs.tid + k * NCT;
+            v[k] = i < HIDDEN ? __bfloat162float(__ldg(p + i)) : 0.f;
+        }
+    }
+};
+
+// RMSNorm of src[1024] (fp32, smem) -> dst (smem) over the consumer threads:
+// x * rsqrt(mean(x^2) + eps) * w  (int8_decoder.py:228-232).  The weight is
+// already in registers (NormW), so no global load sits on the critical path.
+__device__ __forceinline__ void rmsnorm_1024(Cons& cs, const float* src, const NormW& w, float* dst) {
     float ss = 0.f;
-    for (int i = cs.tid; i < HIDDEN; i += NCT) ss += src[i] * src[i];
+#pragma unroll
+    for (int k = 0; k < NORM_PER; ++k) {
+        const int i = cs.tid + k * NCT;
+        if (i < HIDDEN) ss += src[i] * src[i];
+    }
     ss = warp_sum(ss);
     if (cs.lane == 0) cs.sm->red[cs.warp] = ss;
     consumers_sync();
@@ -349,8 +395,56 @@ __device__ __forceinline__ void rmsnorm_1024(Cons& cs, const float* src, const _
 #pragma unroll
     for (int i = 0; i < NCW; ++i) tot += cs.sm->red[i];
     const float rstd = rsqrtf(tot / (float)HIDDEN + RMS_EPS);
-    for (int i = cs.tid; i < HIDDEN; i += NCT) dst[i] = src[i] * rstd * __bfloat162float(w[i]);
+#pragma unroll
+    for (int k = 0; k < NORM_PER; ++k) {
+        const int i = cs.tid + k * NCT;
+        if (i < HIDDEN) dst[i] = src[i] * rstd * w.v[k];
+    }
     consumers_sync();
+}
+
+// Gather n tagged words addr(0..n) into the consumer threads: thread t owns
+// indices t, t + NCT, ...; all of its loads are issued together and only the
+// words whose tag has not arrived are re-read.  store(i, payload) per word.
+template <int MAXK, class Addr, class Store>
+__device__ __forceinline__ void poll_gather(Ctx& c, const Cons& cs, Addr addr, int n, uint32_t tag, int where,
+                                            Store store) {
+    dbg(400 + where);
+    uint64_t v[MAXK];
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+        const int i = cs.tid + k * NCT;
+        v[k] = i < n ? ld_relaxed64(addr(i)) : ((uint64_t)tag << 32);
+    }
+    bool done = false;
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0; !done; ++it) {
+        done = true;
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+            if ((uint32_t)(v[k] >> 32) != tag) {
+                done = false;
+                v[k] = ld_relaxed64(addr(cs.tid + k * NCT));
+            }
+        }
+        if (!done && (it & 127) == 127) {
+            if (t0 == 0) t0 = globaltimer();
+            if (aborted(c)) break;
+            if (globaltimer() - t0 > c.budget) { record_error(c, MQ_DEV_TIMEOUT_EXCHANGE, where); break; }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+        const int i = cs.tid + k * NCT;
+        if (i < n) store(i, (uint32_t)v[k]);
+    }
+    dbg(500 + where);
+}
+
+template <int MAXK, class Store>
+__device__ __forceinline__ void poll_block(Ctx& c, const Cons& cs, const uint64_t* base, int n, uint32_t tag,
+                                           int where, Store store) {
+    poll_gather<MAXK>(c, cs, [&](int i) { return base + i; }, n, tag, where, store);
 }
 
 __device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layer, int e) {
@@ -407,12 +501,24 @@ __device__ __forceinline__ void attn_block(Cons& cs, const uint16_t* kb, const u
     consumers_sync();
 }
 
-// QK RMSNorm over one 128-wide head then split-half RoPE at `pos`
+// QK RMSNorm over one 128-wide head then split-half RoPE at the current position
 // (a10_int8_decode_kernel.cu:160-192, int8_decoder.py:234-240).  Lane holds
 // dims lane + 32j, so the RoPE partners (i, i+64) are j and j+2 of one lane.
-__device__ __forceinline__ void qk_norm_rope(const float* raw, const __nv_bfloat16* nw,
-                                             const __nv_bfloat16* cosr, const __nv_bfloat16* sinr,
-                                             int lane, float out[4]) {
+// Norm weights and the cos/sin row are loaded ahead of the exchange wait.
+struct RopeRegs {
+    float nw[4], cs[4], sn[4];
+    __device__ __forceinline__ void load(const void* normw, const __nv_bfloat16* cosr, const __nv_bfloat16* sinr,
+                                         int lane) {
+        const __nv_bfloat16* w = (const __nv_bfloat16*)normw;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            nw[j] = __bfloat162float(__ldg(w + lane + 32 * j));
+            cs[j] = __bfloat162float(__ldg(cosr + lane + 32 * j));
+            sn[j] = __bfloat162float(__ldg(sinr + lane + 32 * j));
+        }
+    }
+};
+__device__ __forceinline__ void qk_norm_rope(const float* raw, const RopeRegs& R, int lane, float out[4]) {
     float v[4];
     float ss = 0.f;
 #pragma unroll
@@ -420,41 +526,41 @@ __device__ __forceinline__ void qk_norm_rope(const float* raw, const __nv_bfloat
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)HD + RMS_EPS);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * __bfloat162float(nw[lane + 32 * j]);
+    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * R.nw[j];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-        const int i = lane + 32 * j;
-        out[j] = v[j] * __bfloat162float(cosr[i]) - v[j + 2] * __bfloat162float(sinr[i]);
-        out[j + 2] = v[j] * __bfloat162float(sinr[i + 64]) + v[j + 2] * __bfloat162float(cosr[i + 64]);
+        out[j] = v[j] * R.cs[j] - v[j + 2] * R.sn[j];
+        out[j + 2] = v[j] * R.sn[j + 2] + v[j + 2] * R.cs[j + 2];
     }
 }
 
-__device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo& G, int l,
-                               const LayerWeights& w, uint32_t epoch) {
+__device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo& G, int l, uint32_t epoch) {
     Smem* sm = cs.sm;
     const int par = l & 1;
     const uint32_t tq = tag_of(epoch, l, E_QKV);
-    // raw q (two heads), k, v of KV head g
-    for (int i = cs.tid; i < 4 * HD; i += NCT) {
-        int src;
-        if (i < 2 * HD) src = 2 * G.g * HD + i;
-        else if (i < 3 * HD) src = QSZ + G.g * HD + (i - 2 * HD);
-        else src = QSZ + KVSZ + G.g * HD + (i - 3 * HD);
-        sm->raw[i] = __uint_as_float(poll_word(c, &c.ws->xqkv[par][src], tq, 10));
+    const int pos = G.c - 1;
+    RopeRegs R;
+    if (cs.warp < 3)  // warps 0,1: q heads (q_norm); warp 2: k head (k_norm)
+        R.load(sm->lw[l][cs.warp < 2 ? 4 : 5], P.cos_t + (size_t)pos * HD, P.sin_t + (size_t)pos * HD, cs.lane);
+    // raw q (two heads), k, v of KV head g: three runs of the q|k|v row space, one gathered poll
+    {
+        const uint64_t* xq = c.ws->xqkv[par];
+        const int g = G.g;
+        poll_gather<2>(c, cs, [&](int i) {
+            return xq + (i < 2 * HD ? 2 * g * HD + i
+                                    : (i < 3 * HD ? QSZ + g * HD + (i - 2 * HD) : QSZ + KVSZ + g * HD + (i - 3 * HD)));
+        }, 4 * HD, tq, 10, [&](int i, uint32_t p) { sm->raw[i] = __uint_as_float(p); });
     }
     if (cs.tid < 2) { sm->m[cs.tid] = -INFINITY; sm->l[cs.tid] = 0.f; }
     consumers_sync();
-    const int pos = G.c - 1;
-    const __nv_bfloat16* cosr = P.cos_t + (size_t)pos * HD;
-    const __nv_bfloat16* sinr = P.sin_t + (size_t)pos * HD;
     if (cs.warp < 2) {
         float o[4];
-        qk_norm_rope(sm->raw + cs.warp * HD, (const __nv_bfloat16*)w.q_norm_weight, cosr, sinr, cs.lane, o);
+        qk_norm_rope(sm->raw + cs.warp * HD, R, cs.lane, o);
 #pragma unroll
         for (int j = 0; j < 4; ++j) sm->q[cs.warp][cs.lane + 32 * j] = o[j];
     } else if (cs.warp == 2 && G.owner) {
         float o[4];
-        qk_norm_rope(sm->raw + 2 * HD, (const __nv_bfloat16*)w.k_norm_weight, cosr, sinr, cs.lane, o);
+        qk_norm_rope(sm->raw + 2 * HD, R, cs.lane, o);
         const size_t off = (((size_t)l * NKVH + G.g) * (size_t)P.max_seq + pos) * HD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -518,6 +624,56 @@ __device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Ge
 // ---------------------------------------------------------------------------
 // Consumer main: the layer loop.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void trace_stamp(const DecodeParams& P, const Cons& cs, int slot) {
+    if (P.trace && cs.tid == 0 && slot < P.trace_slots)
+        P.trace[(size_t)blockIdx.x * P.trace_slots + slot] = globaltimer();
+}
+
+enum { LW_IN = 0, LW_Q, LW_K, LW_V, LW_QN, LW_KN, LW_O, LW_POST, LW_G, LW_U, LW_D };
+enum { LS_Q = 0, LS_K, LS_V, LS_O, LS_G, LS_U, LS_D };
+
+// Pointer tables of every layer into shared memory (one dependent global load
+// per pointer at kernel start instead of one per phase).
+__device__ __forceinline__ void stage_pointers(const DecodeParams& P, const Cons& cs, bool scaled) {
+    const int per = scaled ? 18 : 11;
+    for (int i = cs.tid; i < P.L * per; i += NCT) {
+        const int l = i / per, f = i % per;
+        if (f < 11) cs.sm->lw[l][f] = reinterpret_cast<const void* const*>(&P.layers[l])[f];
+        else cs.sm->ls[l][f - 11] = reinterpret_cast<float* const*>(&P.scales[l])[f - 11];
+    }
+}
+
+// Every per-row scale this CTA will need in the step, into shared memory, so
+// that no matvec row waits on a dependent global load.  Needs the staged
+// pointer tables (call after stage_pointers + a consumer barrier).
+__device__ __forceinline__ void stage_scales(const DecodeParams& P, const Cons& cs, const Geo& G) {
+    Smem* sm = cs.sm;
+    for (int i = cs.tid; i < P.L * SCL_STRIDE; i += NCT) {
+        const int l = i / SCL_STRIDE, j = i % SCL_STRIDE;
+        float v = 0.f;
+        if (j < SCL_O) {
+            const int r = G.qkv0 + j;
+            if (r < G.qkv1)
+                v = __ldg(r < QSZ ? sm->ls[l][LS_Q] + r
+                                  : (r < QSZ + KVSZ ? sm->ls[l][LS_K] + (r - QSZ) : sm->ls[l][LS_V] + (r - QSZ - KVSZ)));
+        } else if (j < SCL_G) {
+            const int r = G.o0 + (j - SCL_O);
+            if (r < G.o1) v = __ldg(sm->ls[l][LS_O] + r);
+        } else if (j < SCL_U) {
+            const int r = G.gu0 + (j - SCL_G);
+            if (r < G.gu1) v = __ldg(sm->ls[l][LS_G] + r);
+        } else if (j < SCL_D) {
+            const int r = G.gu0 + (j - SCL_U);
+            if (r < G.gu1) v = __ldg(sm->ls[l][LS_U] + r);
+        } else {
+            const int r = G.d0 + (j - SCL_D);
+            if (r < G.d1) v = __ldg(sm->ls[l][LS_D] + r);
+        }
+        sm->scl[i] = v;
+    }
+    for (int j = cs.tid; j < G.lm1 - G.lm0; j += NCT) sm->lm_scl[j] = __ldg(P.lm_scale + G.lm0 + j);
+}
+
 template <class WT>
 __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint32_t epoch, int token,
                               unsigned long long& cta_key) {
@@ -525,109 +681,116 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
     Workspace* ws = c.ws;
     const bool cta0 = G.b == 0;
+    stage_pointers(P, cs, WT::HAS_SCALE);
+    consumers_sync();
+    if (WT::HAS_SCALE) stage_scales(P, cs, G);
+    NormW w_in, w_post;
+    w_in.load(cs, sm->lw[0][LW_IN]);
     if (!*(volatile int*)&sm->abort_flag) {
         const __nv_bfloat16* er = (const __nv_bfloat16*)P.embed + (size_t)token * HIDDEN;
         for (int i = cs.tid; i < HIDDEN; i += NCT) sm->h[i] = __bfloat162float(er[i]);
     }
     for (int l = 0; l < P.L; ++l) {
         const int par = l & 1;
-        const LayerWeights& w = P.layers[l];
+        const int tb = l * TRACE_PER_LAYER;
         if (consumers_sync_abort(c)) break;
         if (l > 0) {
-            const uint32_t t = tag_of(epoch, l, E_H);
-            for (int i = cs.tid; i < HIDDEN; i += NCT) {
-                sm->h[i] = bf16_bits_to_f32(poll_word(c, &ws->xh[par][i], t, 20));
-                if (cta0 && P.layer_hidden) P.layer_hidden[(size_t)(l - 1) * HIDDEN + i] = sm->h[i];
-            }
-        }
-        rmsnorm_1024(cs, sm->h, (const __nv_bfloat16*)w.input_layernorm_weight, sm->x);
-        // --- QKV ---
-        {
-            const ScalePointers* sp = WT::HAS_SCALE ? &P.scales[l] : nullptr;
-            const uint32_t t = tag_of(epoch, l, E_QKV);
-            const bool skip = (l == 0 && G.b == P.skip_cta);
-            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, [&](int r, float d) {
-                if (WT::HAS_SCALE) {
-                    const float s = r < QSZ ? sp->q_scale[r] : (r < QSZ + KVSZ ? sp->k_scale[r - QSZ] : sp->v_scale[r - QSZ - KVSZ]);
-                    d *= s;
-                }
-                if (!skip) st_tagged(&ws->xqkv[par][r], t, __float_as_uint(d));
+            float* lh = (cta0 && P.layer_hidden) ? P.layer_hidden + (size_t)(l - 1) * HIDDEN : nullptr;
+            poll_block<NORM_PER>(c, cs, ws->xh[par], HIDDEN, tag_of(epoch, l, E_H), 20, [&](int i, uint32_t p) {
+                const float v = bf16_bits_to_f32(p);
+                sm->h[i] = v;
+                if (lh) lh[i] = v;
             });
         }
+        trace_stamp(P, cs, tb + TR_START);
+        rmsnorm_1024(cs, sm->h, w_in, sm->x);
+        w_post.load(cs, sm->lw[l][LW_POST]);  // needed after attention: its latency is hidden
+        const float* lsc = sm->scl + l * SCL_STRIDE;
+        // --- QKV ---
+        {
+            const uint32_t t = tag_of(epoch, l, E_QKV);
+            const bool skip = (l == 0 && G.b == P.skip_cta);
+            uint64_t* dst = ws->xqkv[par];
+            auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[r - G.qkv0] : 1.f; };
+            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, scl, [&](int r, float d) {
+                if (!skip) st_tagged(&dst[r], t, __float_as_uint(d));
+            });
+        }
+        trace_stamp(P, cs, tb + TR_QKV);
         // --- attention (only CTAs that own an item) ---
         if (G.item >= 0) {
             if (consumers_sync_abort(c)) break;
-            attention_item(P, c, cs, G, l, w, epoch);
+            attention_item(P, c, cs, G, l, epoch);
+            trace_stamp(P, cs, tb + TR_ATTN);
         }
         // --- O projection + residual ---
         if (consumers_sync_abort(c)) break;
-        {
-            const uint32_t t = tag_of(epoch, l, E_ATTN);
-            for (int i = cs.tid; i < QSZ; i += NCT) sm->x[i] = __uint_as_float(poll_word(c, &ws->xattn[par][i], t, 30));
-        }
+        poll_block<QSZ / NCT + 1>(c, cs, ws->xattn[par], QSZ, tag_of(epoch, l, E_ATTN), 30,
+                                  [&](int i, uint32_t p) { sm->x[i] = __uint_as_float(p); });
         consumers_sync();
+        trace_stamp(P, cs, tb + TR_OIN);
         {
-            const float* so = WT::HAS_SCALE ? P.scales[l].o_scale : nullptr;
             const uint32_t t = tag_of(epoch, l, E_ACT);
-            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, [&](int r, float d) {
-                if (WT::HAS_SCALE) d *= so[r];
-                st_tagged(&ws->xact[par][r], t, __float_as_uint(d + sm->h[r]));
+            uint64_t* dst = ws->xact[par];
+            auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_O + r - G.o0] : 1.f; };
+            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, scl, [&](int r, float d) {
+                st_tagged(&dst[r], t, __float_as_uint(d + sm->h[r]));
             });
         }
+        trace_stamp(P, cs, tb + TR_O);
         // --- post-attention norm + gate/up ---
         if (consumers_sync_abort(c)) break;
+        poll_block<NORM_PER>(c, cs, ws->xact[par], HIDDEN, tag_of(epoch, l, E_ACT), 40,
+                             [&](int i, uint32_t p) { sm->act[i] = __uint_as_float(p); });
+        rmsnorm_1024(cs, sm->act, w_post, sm->x);
+        w_in.load(cs, l + 1 < P.L ? sm->lw[l + 1][LW_IN] : P.final_norm);  // next norm, loaded ahead
+        trace_stamp(P, cs, tb + TR_NORM2);
         {
-            const uint32_t t = tag_of(epoch, l, E_ACT);
-            for (int i = cs.tid; i < HIDDEN; i += NCT) sm->act[i] = __uint_as_float(poll_word(c, &ws->xact[par][i], t, 40));
-        }
-        rmsnorm_1024(cs, sm->act, (const __nv_bfloat16*)w.post_attn_layernorm_weight, sm->x);
-        {
-            const float* sg = WT::HAS_SCALE ? P.scales[l].gate_scale : nullptr;
-            const float* su = WT::HAS_SCALE ? P.scales[l].up_scale : nullptr;
             const uint32_t t = tag_of(epoch, l, E_MLP);
-            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, [&](int r, float gd, float ud) {
-                if (WT::HAS_SCALE) { gd *= sg[r]; ud *= su[r]; }
+            uint64_t* dst = ws->xmlp[par];
+            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, lsc + SCL_G, lsc + SCL_U, [&](int r, float gd, float ud) {
                 const float silu = gd / (1.0f + expf(-gd));
-                st_tagged(&ws->xmlp[par][r], t, __float_as_uint(silu * ud));
+                st_tagged(&dst[r], t, __float_as_uint(silu * ud));
             });
         }
+        trace_stamp(P, cs, tb + TR_GU);
         // --- down + residual -> next h (bf16) ---
         if (consumers_sync_abort(c)) break;
-        {
-            const uint32_t t = tag_of(epoch, l, E_MLP);
-            for (int i = cs.tid; i < INTER; i += NCT) sm->x[i] = __uint_as_float(poll_word(c, &ws->xmlp[par][i], t, 50));
-        }
+        poll_block<INTER / NCT>(c, cs, ws->xmlp[par], INTER, tag_of(epoch, l, E_MLP), 50,
+                                [&](int i, uint32_t p) { sm->x[i] = __uint_as_float(p); });
         consumers_sync();
+        trace_stamp(P, cs, tb + TR_MLPIN);
         {
-            const float* sd = WT::HAS_SCALE ? P.scales[l].down_scale : nullptr;
             const uint32_t t = tag_of(epoch, l + 1, E_H);
             uint64_t* dst = ws->xh[(l + 1) & 1];
-            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, [&](int r, float d) {
-                if (WT::HAS_SCALE) d *= sd[r];
+            auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_D + r - G.d0] : 1.f; };
+            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, scl, [&](int r, float d) {
                 st_tagged(&dst[r], t, f32_to_bf16_bits(d + sm->act[r]));
             });
         }
+        trace_stamp(P, cs, tb + TR_DOWN);
     }
     // --- final norm + LM head + argmax ---
     cta_key = 0ull;
     if (consumers_sync_abort(c)) return;
     {
-        const uint32_t t = tag_of(epoch, P.L, E_H);
-        for (int i = cs.tid; i < HIDDEN; i += NCT) {
-            sm->h[i] = bf16_bits_to_f32(poll_word(c, &ws->xh[P.L & 1][i], t, 60));
-            if (cta0 && P.layer_hidden) P.layer_hidden[(size_t)(P.L - 1) * HIDDEN + i] = sm->h[i];
-        }
+        float* lh = (cta0 && P.layer_hidden) ? P.layer_hidden + (size_t)(P.L - 1) * HIDDEN : nullptr;
+        poll_block<NORM_PER>(c, cs, ws->xh[P.L & 1], HIDDEN, tag_of(epoch, P.L, E_H), 60, [&](int i, uint32_t p) {
+            const float v = bf16_bits_to_f32(p);
+            sm->h[i] = v;
+            if (lh) lh[i] = v;
+        });
     }
-    rmsnorm_1024(cs, sm->h, (const __nv_bfloat16*)P.final_norm, sm->x);
+    trace_stamp(P, cs, P.L * TRACE_PER_LAYER + 0);
+    rmsnorm_1024(cs, sm->h, w_in, sm->x);
     if (cta0 && P.g_normalized)
         for (int i = cs.tid; i < HIDDEN; i += NCT) P.g_normalized[i] = sm->x[i];
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     {
-        const float* ls = P.lm_scale;
         float* logits = P.logits;
-        mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, [&](int r, float d) {
-            if (WT::HAS_SCALE) d *= ls[r];
+        auto scl = [&](int r) { return WT::HAS_SCALE ? sm->lm_scl[r - G.lm0] : 1.f; };
+        mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, [&](int r, float d) {
             if (logits) logits[r] = d;
             if (d > best_v) { best_v = d; best_i = r; }
         });
@@ -637,6 +800,7 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
                            : (((unsigned long long)float_order_key(best_v)) << 32) | (uint32_t)(~(uint32_t)best_i);
     }
     consumers_sync();
+    trace_stamp(P, cs, P.L * TRACE_PER_LAYER + 1);
     if (cs.tid == 0) {
         unsigned long long k = 0ull;
         for (int i = 0; i < NCW; ++i) k = sm->best[i] > k ? sm->best[i] : k;
@@ -733,10 +897,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) matvec_kernel(const MatvecParams 
         Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
         const float* sc = P.scale;
         float* y = P.y;
-        mv_phase<WT, K>(c, cs, r0, r1, sm->x, [&](int r, float d) {
-            if (WT::HAS_SCALE) d *= sc[r];
-            y[r] = d;
-        });
+        auto scl = [&](int r) { return WT::HAS_SCALE ? __ldg(sc + r) : 1.f; };
+        mv_phase<WT, K>(c, cs, r0, r1, sm->x, scl, [&](int r, float d) { y[r] = d; });
     }
     __syncthreads();
 }
@@ -757,6 +919,8 @@ DevState g_dev[MAX_DEV];
 unsigned long long g_budget_ns = 2000000000ull;
 int g_skip_cta = -1;
 int g_pos_per_split = 256;
+unsigned long long* g_trace = nullptr;
+int g_trace_slots = 0;
 
 int dev_state(DevState** out) {
     int dev = 0;
@@ -767,7 +931,7 @@ int dev_state(DevState** out) {
     if (!d.ws) {
         int sms = 0;
         if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return (int)e;
-        if (sms < NKVH) return MQ_ERR_DEVICE;
+        if (sms < MIN_CTAS) return MQ_ERR_DEVICE;
         Workspace* ws = nullptr;
         if ((e = cudaMalloc(&ws, sizeof(Workspace))) != cudaSuccess) return (int)e;
         if ((e = cudaMemset(ws, 0, sizeof(Workspace))) != cudaSuccess) return (int)e;
@@ -810,6 +974,8 @@ int launch_step(int kind, DecodeParams& P, cudaStream_t stream) {
     P.ws = d->ws;
     P.budget_ns = g_budget_ns;
     P.skip_cta = g_skip_cta;
+    P.trace = g_trace;
+    P.trace_slots = g_trace_slots;
     g_skip_cta = -1;
     P.splits = choose_splits(P.position + 1, d->num_sms);
     // Tags are 32-bit epochs; clear the hand-off buffers long before they wrap.
@@ -839,6 +1005,7 @@ int check_common(const void* embed, const LayerWeights* lw, const void* fnorm, c
     if (!embed || !lw || !fnorm || !lm || !cos_t || !sin_t || !kc || !vc) return MQ_ERR_ARG;
     if (!aligned16(lm) || !aligned16(kc) || !aligned16(vc) || !aligned16(embed)) return MQ_ERR_ARG;
     if (L <= 0 || max_seq <= 0) return MQ_ERR_ARG;
+    if (L > MAX_LAYERS) return MQ_ERR_SIZE;
     if (position < 0 || position >= max_seq) return MQ_ERR_POSITION;
     return 0;
 }
@@ -995,5 +1162,20 @@ extern "C" int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads) {
     if (num_ctas) *num_ctas = e == cudaSuccess ? sms : 0;
     if (smem_bytes) *smem_bytes = (int)sizeof(Smem);
     if (threads) *threads = NTHREADS;
+    return (int)e;
+}
+
+extern "C" int mq_set_trace(unsigned long long* dev_buf, int slots_per_cta) {
+    if (dev_buf && slots_per_cta <= 0) return MQ_ERR_ARG;
+    g_trace = dev_buf;
+    g_trace_slots = dev_buf ? slots_per_cta : 0;
+    return 0;
+}
+
+// Development aid, not part of the public header: stamp buffer of MQ_DEBUG_STAMPS builds.
+extern "C" int mqdbg_set_stamp_buffer(unsigned long long* buf) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyToSymbol(g_dbg_buf, &buf, sizeof(buf));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_dbg_n, &zero, sizeof(zero));
     return (int)e;
 }

@@ -22,6 +22,7 @@ MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 
 EXPORTED = (
     "launch_a10_int8_decode", "launch_a10_decode", "mq_decode_multi", "mq_quantize_per_channel",
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
+    "mq_set_trace",
 )
 
 
@@ -65,6 +66,7 @@ def load():
     lib.mq_device_status.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), _i]
     lib.mq_set_wait_budget_ns.argtypes = [_u64]
     lib.mq_inject_skip_publish.argtypes = [_i, _i]
+    lib.mq_set_trace.argtypes = [_vp, _i]
     lib.mq_kernel_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
     for name in EXPORTED:
         getattr(lib, name).restype = _i
@@ -105,3 +107,9 @@ def kernel_info():
     a, b, c = _i(0), _i(0), _i(0)
     load().mq_kernel_info(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
     return {"num_ctas": a.value, "smem_bytes": b.value, "threads": c.value}
+
+
+def set_trace(buf=None, slots_per_cta=0):
+    """buf: device int64 tensor [num_ctas, slots_per_cta], or None to disable."""
+    ptr = ctypes.c_void_p(buf.data_ptr() if buf is not None else 0)
+    check(load().mq_set_trace(ptr, int(slots_per_cta) if buf is not None else 0), "mq_set_trace")

@@ -28,7 +28,7 @@ constexpr int NCW = 12;                       // consumer warps
 constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
 constexpr int STAGE_BYTES = 16384;
-constexpr int NSTAGE = 11;
+constexpr int NSTAGE = 10;
 constexpr int KV_CHUNK_POS = STAGE_BYTES / (2 * HD * 2);  // 32 positions of K then V
 constexpr int MAX_SPLITS = 18;                // attention splits per KV head
 constexpr int MAX_LAYERS = 32;                // pointer/scale tables staged in shared memory
@@ -134,6 +134,7 @@ __device__ __forceinline__ uint32_t float_order_key(float f) {
 struct W8 {
     static constexpr int EPU = 16;  // int8 elements per 16-byte unit
     static constexpr bool HAS_SCALE = true;
+    static constexpr bool LIMBS = true;   // matvecs use the Limbs dp4a path
     // int8 -> fp32 exactly: byte^0x80 placed in the mantissa of 2^23, minus 2^23+128.
     __device__ __forceinline__ static void dot(const uint4 w, const float* x, float& a0, float& a1) {
         const uint32_t ws[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
@@ -149,9 +150,68 @@ struct W8 {
         }
     }
 };
+// Exact-integer INT8 dot product against fp32 activations.  Once per matvec
+// phase the CTA scales the activation vector by one power of two 2^k (chosen
+// so max|x| * 2^k < 2^22), rounds to integers X and splits each X into three
+// signed 8-bit limbs, X = X2*2^16 + X1*2^8 + X0 (packed 4 per word, in shared
+// memory).  A 16-byte weight unit then costs three dp4a per 4-byte word with
+// exact int32 accumulation; each lane's partial sum is recombined exactly in
+// fp64 and scaled back by 2^-k before the fp32 warp reduction.  The only
+// rounding beyond fp32 summation is that of x to 22 bits relative to max|x|.
+__device__ __forceinline__ void limb_split(float x, float up, uint32_t& p0, uint32_t& p1, uint32_t& p2, int b) {
+    const int X = __float2int_rn(x * up);
+    const int d0 = ((X + 128) & 255) - 128;
+    const int r = (X - d0) >> 8;
+    const int d1 = ((r + 128) & 255) - 128;
+    const int d2 = (r - d1) >> 8;
+    p0 |= (uint32_t)(d0 & 255) << (8 * b);
+    p1 |= (uint32_t)(d1 & 255) << (8 * b);
+    p2 |= (uint32_t)(d2 & 255) << (8 * b);
+}
+// Power-of-two scale for max|x| = m: returns 2^k, sets inv = 2^-k.
+__device__ __forceinline__ float limb_scale(float m, float& inv) {
+    int e = 0;
+    frexpf(m, &e);                      // m < 2^e
+    int k = m > 0.f ? 22 - e : 0;
+    k = max(-126, min(126, k));
+    inv = __int_as_float((127 - k) << 23);
+    return __int_as_float((127 + k) << 23);
+}
+template <int NW>   // NW = 4-byte activation words per lane (K / 128)
+struct Limbs {
+    int l0[NW], l1[NW], l2[NW];
+    float inv;  // 2^-k
+    // Loads this lane's words: unit j of the lane covers words 4*(lane+32j) .. +3.
+    __device__ __forceinline__ void load(const int* L0, const int* L1, const int* L2, int lane, float inv_) {
+        inv = inv_;
+#pragma unroll
+        for (int j = 0; j < NW / 4; ++j) {
+            const int w = 4 * (lane + 32 * j);
+            const int4 a = *reinterpret_cast<const int4*>(L0 + w);
+            const int4 b = *reinterpret_cast<const int4*>(L1 + w);
+            const int4 c = *reinterpret_cast<const int4*>(L2 + w);
+            l0[4 * j] = a.x; l0[4 * j + 1] = a.y; l0[4 * j + 2] = a.z; l0[4 * j + 3] = a.w;
+            l1[4 * j] = b.x; l1[4 * j + 1] = b.y; l1[4 * j + 2] = b.z; l1[4 * j + 3] = b.w;
+            l2[4 * j] = c.x; l2[4 * j + 1] = c.y; l2[4 * j + 2] = c.z; l2[4 * j + 3] = c.w;
+        }
+    }
+    // Dot of this lane's limbs with the int8 weights of unit j (words 4j..4j+3).
+    __device__ __forceinline__ void acc(const uint4 w, int j, int& a0, int& a1, int& a2) const {
+        a0 = __dp4a((int)w.x, l0[4 * j + 0], a0); a1 = __dp4a((int)w.x, l1[4 * j + 0], a1); a2 = __dp4a((int)w.x, l2[4 * j + 0], a2);
+        a0 = __dp4a((int)w.y, l0[4 * j + 1], a0); a1 = __dp4a((int)w.y, l1[4 * j + 1], a1); a2 = __dp4a((int)w.y, l2[4 * j + 1], a2);
+        a0 = __dp4a((int)w.z, l0[4 * j + 2], a0); a1 = __dp4a((int)w.z, l1[4 * j + 2], a1); a2 = __dp4a((int)w.z, l2[4 * j + 2], a2);
+        a0 = __dp4a((int)w.w, l0[4 * j + 3], a0); a1 = __dp4a((int)w.w, l1[4 * j + 3], a1); a2 = __dp4a((int)w.w, l2[4 * j + 3], a2);
+    }
+    __device__ __forceinline__ float finish(int a0, int a1, int a2) const {
+        const double v = fma((double)a2, 65536.0, fma((double)a1, 256.0, (double)a0));  // exact (< 2^53)
+        return (float)v * inv;
+    }
+};
+
 struct W16 {
     static constexpr int EPU = 8;  // bf16 elements per 16-byte unit
     static constexpr bool HAS_SCALE = false;
+    static constexpr bool LIMBS = false;
     __device__ __forceinline__ static void dot(const uint4 w, const float* x, float& a0, float& a1) {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll

@@ -66,6 +66,9 @@ struct Smem {
     float act[HIDDEN];       // h + O (residual of the MLP half)
     float x[INTER];          // current matvec activation (normalized / attn / mlp)
     float red[NCW];
+    float red2[NCW];
+    float limb_inv;
+    alignas(16) int limb[3][INTER / 4];  // activation limbs of the current matvec phase (int4 loads)
     float raw[4 * HD];       // raw q0 q1 k v of this CTA's KV head
     float q[2][HD];
     float m[2], l[2], corr[2];

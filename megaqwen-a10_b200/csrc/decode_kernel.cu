@@ -31,10 +31,15 @@ __device__ int g_dbg_n;
 __device__ unsigned long long* g_dbg_buf;
 __device__ __forceinline__ void dbg(int id) {
 #if MQ_DEBUG_STAMPS
-    if (blockIdx.x == 1 && threadIdx.x == 0 && g_dbg_buf && g_dbg_n < 4000) {
-        g_dbg_buf[2 * g_dbg_n] = id;
-        g_dbg_buf[2 * g_dbg_n + 1] = clock64();
-        ++g_dbg_n;
+    __shared__ int s_n;  // set to 0 by dbg(-1) at kernel start
+    if (blockIdx.x == 1 && threadIdx.x == 0) {
+        const long long t = clock64();
+        if (id < 0) { s_n = 0; return; }
+        if (g_dbg_buf && s_n < 4000) {
+            g_dbg_buf[2 * s_n] = id;
+            g_dbg_buf[2 * s_n + 1] = t;
+            ++s_n;
+        }
     }
 #else
     (void)id;
@@ -284,21 +289,53 @@ struct Cons {
 // Matvec over rows [r0, r1) of one projection streamed through the ring.
 // Row i (phase-relative) is handled by warp i % NCW; lane holds the activation
 // elements of its fixed 16-byte units in registers for the whole phase.
+// Builds the limbs of x_s[0..n) into shared memory (all consumer threads; the
+// caller guarantees x_s is complete).  Two consumer barriers.
+__device__ __forceinline__ void build_limbs(Cons& cs, const float* x_s, int n) {
+    Smem* sm = cs.sm;
+    float m = 0.f;
+    for (int i = cs.tid; i < n; i += NCT) m = fmaxf(m, fabsf(x_s[i]));
+    m = warp_max(m);
+    if (cs.lane == 0) sm->red2[cs.warp] = m;
+    consumers_sync();
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) m = fmaxf(m, sm->red2[i]);
+    float inv;
+    const float up = limb_scale(m, inv);
+    for (int w = cs.tid; w < n / 4; w += NCT) {
+        const float4 v = *reinterpret_cast<const float4*>(x_s + 4 * w);
+        uint32_t p0 = 0, p1 = 0, p2 = 0;
+        limb_split(v.x, up, p0, p1, p2, 0);
+        limb_split(v.y, up, p0, p1, p2, 1);
+        limb_split(v.z, up, p0, p1, p2, 2);
+        limb_split(v.w, up, p0, p1, p2, 3);
+        sm->limb[0][w] = (int)p0; sm->limb[1][w] = (int)p1; sm->limb[2][w] = (int)p2;
+    }
+    if (cs.tid == 0) sm->limb_inv = inv;
+    consumers_sync();
+}
+
 template <class WT, int K, class Scl, class Out>
 __device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
     constexpr int RPC = STAGE_BYTES / RB;
-    float xr[UPL * WT::EPU];
+    float xr[WT::LIMBS ? 1 : UPL * WT::EPU];
+    Limbs<WT::LIMBS ? UPL * 4 : 4> lb;
+    if constexpr (WT::LIMBS) {
+        build_limbs(cs, x_s, K);
+        lb.load(cs.sm->limb[0], cs.sm->limb[1], cs.sm->limb[2], cs.lane, cs.sm->limb_inv);
+    } else {
 #pragma unroll
-    for (int j = 0; j < UPL; ++j) {
-        const int e0 = (cs.lane + 32 * j) * WT::EPU;
+        for (int j = 0; j < UPL; ++j) {
+            const int e0 = (cs.lane + 32 * j) * WT::EPU;
 #pragma unroll
-        for (int e = 0; e < WT::EPU; e += 4) {
-            float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
-            xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
-            xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+            for (int e = 0; e < WT::EPU; e += 4) {
+                float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
+                xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
+                xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+            }
         }
     }
     const int n = r1 - r0;
@@ -309,10 +346,19 @@ __device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const
         for (; i < ce; i += NCW) {
             const float sc = scl(r0 + i);
             const uint4* row = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
-            float a0 = 0.f, a1 = 0.f;
+            float part;
+            if constexpr (WT::LIMBS) {
+                int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
-            for (int j = 0; j < UPL; ++j) WT::dot(row[cs.lane + 32 * j], xr + j * WT::EPU, a0, a1);
-            const float dot = warp_sum(a0 + a1);
+                for (int j = 0; j < UPL; ++j) lb.acc(row[cs.lane + 32 * j], j, a0, a1, a2);
+                part = lb.finish(a0, a1, a2);
+            } else {
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < UPL; ++j) WT::dot(row[cs.lane + 32 * j], xr + j * WT::EPU, a0, a1);
+                part = a0 + a1;
+            }
+            const float dot = warp_sum(part);
             if (cs.lane == 0) out(r0 + i, dot * sc);
             dbg(300);
         }
@@ -329,15 +375,21 @@ __device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
     constexpr int RPC = STAGE_BYTES / (2 * RB);
-    float xr[UPL * WT::EPU];
+    float xr[WT::LIMBS ? 1 : UPL * WT::EPU];
+    Limbs<WT::LIMBS ? UPL * 4 : 4> lb;
+    if constexpr (WT::LIMBS) {
+        build_limbs(cs, x_s, K);
+        lb.load(cs.sm->limb[0], cs.sm->limb[1], cs.sm->limb[2], cs.lane, cs.sm->limb_inv);
+    } else {
 #pragma unroll
-    for (int j = 0; j < UPL; ++j) {
-        const int e0 = (cs.lane + 32 * j) * WT::EPU;
+        for (int j = 0; j < UPL; ++j) {
+            const int e0 = (cs.lane + 32 * j) * WT::EPU;
 #pragma unroll
-        for (int e = 0; e < WT::EPU; e += 4) {
-            float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
-            xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
-            xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+            for (int e = 0; e < WT::EPU; e += 4) {
+                float4 v = *reinterpret_cast<const float4*>(x_s + e0 + e);
+                xr[j * WT::EPU + e] = v.x; xr[j * WT::EPU + e + 1] = v.y;
+                xr[j * WT::EPU + e + 2] = v.z; xr[j * WT::EPU + e + 3] = v.w;
+            }
         }
     }
     const int n = r1 - r0;
@@ -351,14 +403,28 @@ __device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const
             if (WT::HAS_SCALE) { gsc = sg[i]; usc = su[i]; }  // phase-relative, shared memory
             const uint4* grow = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
             const uint4* urow = reinterpret_cast<const uint4*>(st + (size_t)(nin + i - cb) * RB);
-            float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+            float gp, up;
+            if constexpr (WT::LIMBS) {
+                int g0 = 0, g1 = 0, g2 = 0, u0 = 0, u1 = 0, u2 = 0;
 #pragma unroll
-            for (int j = 0; j < UPL; ++j) {
-                WT::dot(grow[cs.lane + 32 * j], xr + j * WT::EPU, g0, g1);
-                WT::dot(urow[cs.lane + 32 * j], xr + j * WT::EPU, u0, u1);
+                for (int j = 0; j < UPL; ++j) {
+                    lb.acc(grow[cs.lane + 32 * j], j, g0, g1, g2);
+                    lb.acc(urow[cs.lane + 32 * j], j, u0, u1, u2);
+                }
+                gp = lb.finish(g0, g1, g2);
+                up = lb.finish(u0, u1, u2);
+            } else {
+                float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < UPL; ++j) {
+                    WT::dot(grow[cs.lane + 32 * j], xr + j * WT::EPU, g0, g1);
+                    WT::dot(urow[cs.lane + 32 * j], xr + j * WT::EPU, u0, u1);
+                }
+                gp = g0 + g1;
+                up = u0 + u1;
             }
-            const float gd = warp_sum(g0 + g1);
-            const float ud = warp_sum(u0 + u1);
+            const float gd = warp_sum(gp);
+            const float ud = warp_sum(up);
             if (cs.lane == 0) out(r0 + i, gd * gsc, ud * usc);
         }
         cs.release();
@@ -681,6 +747,7 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
     Workspace* ws = c.ws;
     const bool cta0 = G.b == 0;
+    dbg(-1);
     stage_pointers(P, cs, WT::HAS_SCALE);
     consumers_sync();
     if (WT::HAS_SCALE) stage_scales(P, cs, G);

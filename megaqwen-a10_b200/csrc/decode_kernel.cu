@@ -522,51 +522,6 @@ enum { E_H = 0, E_QKV = 1, E_PART = 2, E_ATTN = 3, E_ACT = 4, E_MLP = 5 };
 // ---------------------------------------------------------------------------
 // Attention for one (KV head g, position split s) item.
 // ---------------------------------------------------------------------------
-// Scores, online-softmax update and V accumulation for n positions whose K rows
-// start at kb and V rows at vb (bf16, HD elements per row, shared memory).
-// Thread t < 256 owns acc for q head (t >> 7) of the pair, dim (t & 127).
-__device__ __forceinline__ void attn_block(Cons& cs, const uint16_t* kb, const uint16_t* vb, int n,
-                                           float scale, float& acc) {
-    Smem* sm = cs.sm;
-    for (int p = cs.warp; p < n; p += NCW) {
-        const uint2 kw = *reinterpret_cast<const uint2*>(kb + p * HD + 4 * cs.lane);
-        const float k0 = bf16_bits_to_f32(kw.x & 0xffffu), k1 = bf16_bits_to_f32(kw.x >> 16);
-        const float k2 = bf16_bits_to_f32(kw.y & 0xffffu), k3 = bf16_bits_to_f32(kw.y >> 16);
-        const float* q0 = sm->q[0] + 4 * cs.lane;
-        const float* q1 = sm->q[1] + 4 * cs.lane;
-        float d0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
-        float d1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
-        d0 = warp_sum(d0);
-        d1 = warp_sum(d1);
-        if (cs.lane == 0) { sm->sc[0][p] = d0 * scale; sm->sc[1][p] = d1 * scale; }
-    }
-    consumers_sync();
-    if (cs.warp < 2) {
-        const int h = cs.warp;
-        const float sv = cs.lane < n ? sm->sc[h][cs.lane] : -INFINITY;
-        const float m_old = sm->m[h];
-        const float m_new = fmaxf(m_old, warp_max(sv));
-        const float pe = cs.lane < n ? expf(sv - m_new) : 0.f;
-        const float sum = warp_sum(pe);
-        sm->pe[h][cs.lane] = pe;
-        __syncwarp();
-        if (cs.lane == 0) {
-            const float corr = expf(m_old - m_new);
-            sm->l[h] = sm->l[h] * corr + sum;
-            sm->m[h] = m_new;
-            sm->corr[h] = corr;
-        }
-    }
-    consumers_sync();
-    if (cs.tid < 2 * HD) {
-        const int h = cs.tid >> 7, d = cs.tid & (HD - 1);
-        float a = acc * sm->corr[h];
-        for (int p = 0; p < n; ++p) a = fmaf(sm->pe[h][p], bf16_bits_to_f32(vb[p * HD + d]), a);
-        acc = a;
-    }
-    consumers_sync();
-}
-
 // QK RMSNorm over one 128-wide head then split-half RoPE at the current position
 // (a10_int8_decode_kernel.cu:160-192, int8_decoder.py:234-240).  Lane holds
 // dims lane + 32j, so the RoPE partners (i, i+64) are j and j+2 of one lane.
@@ -617,7 +572,6 @@ __device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Ge
                                     : (i < 3 * HD ? QSZ + g * HD + (i - 2 * HD) : QSZ + KVSZ + g * HD + (i - 3 * HD)));
         }, 4 * HD, tq, 10, [&](int i, uint32_t p) { sm->raw[i] = __uint_as_float(p); });
     }
-    if (cs.tid < 2) { sm->m[cs.tid] = -INFINITY; sm->l[cs.tid] = 0.f; }
     consumers_sync();
     if (cs.warp < 2) {
         float o[4];
@@ -640,29 +594,89 @@ __device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Ge
         }
     }
     consumers_sync();
-    float acc = 0.f;
+    // Flash-decode inside the CTA without block barriers: warp w owns the item's
+    // positions past0 + t with t % NCW == w and keeps its own online-softmax
+    // state (m, l, acc) for both GQA heads; lane holds dims 4*lane .. 4*lane+3.
+    float q0[4], q1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { q0[j] = sm->q[0][4 * cs.lane + j]; q1[j] = sm->q[1][4 * cs.lane + j]; }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    const float scale = P.attn_scale;
+    auto step = [&](const uint16_t* kr, const uint16_t* vr) {
+        const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * cs.lane);
+        const uint2 vw = *reinterpret_cast<const uint2*>(vr + 4 * cs.lane);
+        const float k[4] = {bf16_bits_to_f32(kw.x & 0xffffu), bf16_bits_to_f32(kw.x >> 16),
+                            bf16_bits_to_f32(kw.y & 0xffffu), bf16_bits_to_f32(kw.y >> 16)};
+        const float v[4] = {bf16_bits_to_f32(vw.x & 0xffffu), bf16_bits_to_f32(vw.x >> 16),
+                            bf16_bits_to_f32(vw.y & 0xffffu), bf16_bits_to_f32(vw.y >> 16)};
+        float d0 = q0[0] * k[0] + q0[1] * k[1] + q0[2] * k[2] + q0[3] * k[3];
+        float d1 = q1[0] * k[0] + q1[1] * k[1] + q1[2] * k[2] + q1[3] * k[3];
+        d0 = warp_sum(d0) * scale;
+        d1 = warp_sum(d1) * scale;
+        const float n0 = fmaxf(m0, d0), n1 = fmaxf(m1, d1);
+        const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);
+        const float e0 = expf(d0 - n0), e1 = expf(d1 - n1);
+        l0 = l0 * c0 + e0;
+        l1 = l1 * c1 + e1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            a0[j] = fmaf(e0, v[j], a0[j] * c0);
+            a1[j] = fmaf(e1, v[j], a1[j] * c1);
+        }
+        m0 = n0;
+        m1 = n1;
+    };
+    int qi = 0;  // item-relative index of the chunk's first position
     for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS) {
         const int n = min(KV_CHUNK_POS, G.past1 - p);
         const uint8_t* st = cs.wait(c, 3);
-        attn_block(cs, reinterpret_cast<const uint16_t*>(st),
-                   reinterpret_cast<const uint16_t*>(st + KV_CHUNK_POS * HD * 2), n, P.attn_scale, acc);
+        const uint16_t* kb = reinterpret_cast<const uint16_t*>(st);
+        const uint16_t* vb = reinterpret_cast<const uint16_t*>(st + KV_CHUNK_POS * HD * 2);
+        for (int t = ((cs.warp - qi) % NCW + NCW) % NCW; t < n; t += NCW) step(kb + t * HD, vb + t * HD);
         cs.release();
+        qi += n;
     }
-    if (G.owner) attn_block(cs, sm->kvcur[0], sm->kvcur[1], 1, P.attn_scale, acc);
-    if (G.S == 1) {
-        if (cs.tid < 2 * HD) {
-            const float o = acc / sm->l[cs.tid >> 7];
-            st_tagged(&c.ws->xattn[par][G.g * 2 * HD + cs.tid], tag_of(epoch, l, E_ATTN), __float_as_uint(o));
+    if (G.owner && qi % NCW == cs.warp) step(sm->kvcur[0], sm->kvcur[1]);  // the current position
+    // Merge the NCW warp states through shared memory (x is free during attention).
+    float* wacc = sm->x;  // [NCW][2][HD]
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        wacc[(cs.warp * 2 + 0) * HD + 4 * cs.lane + j] = a0[j];
+        wacc[(cs.warp * 2 + 1) * HD + 4 * cs.lane + j] = a1[j];
+    }
+    if (cs.lane == 0) {
+        sm->sc[0][cs.warp] = m0; sm->sc[1][cs.warp] = m1;
+        sm->pe[0][cs.warp] = l0; sm->pe[1][cs.warp] = l1;
+    }
+    consumers_sync();
+    float acc = 0.f, M = -INFINITY, L = 0.f;
+    if (cs.tid < 2 * HD) {
+        const int h = cs.tid >> 7, d = cs.tid & (HD - 1);
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) M = fmaxf(M, sm->sc[h][w]);
+#pragma unroll
+        for (int w = 0; w < NCW; ++w) {
+            const float e = expf(sm->sc[h][w] - M);  // 0 for a warp that saw no position
+            L = fmaf(sm->pe[h][w], e, L);
+            acc = fmaf(wacc[(w * 2 + h) * HD + d], e, acc);
         }
+    }
+    if (G.S == 1) {
+        if (cs.tid < 2 * HD)
+            st_tagged(&c.ws->xattn[par][G.g * 2 * HD + cs.tid], tag_of(epoch, l, E_ATTN), __float_as_uint(acc / L));
         return;
     }
     // Split-K: publish (acc, m, l), then merge this split's slice of the pair's 256 outputs.
     const uint32_t tp = tag_of(epoch, l, E_PART);
     uint64_t* part = c.ws->xpart[par];
-    if (cs.tid < 2 * HD) st_tagged(&part[G.item * PART_WORDS + cs.tid], tp, __float_as_uint(acc));
-    if (cs.tid < 2) {
-        st_tagged(&part[G.item * PART_WORDS + 2 * HD + cs.tid], tp, __float_as_uint(sm->m[cs.tid]));
-        st_tagged(&part[G.item * PART_WORDS + 2 * HD + 2 + cs.tid], tp, __float_as_uint(sm->l[cs.tid]));
+    if (cs.tid < 2 * HD) {
+        st_tagged(&part[G.item * PART_WORDS + cs.tid], tp, __float_as_uint(acc));
+        if ((cs.tid & (HD - 1)) == 0) {
+            const int h = cs.tid >> 7;
+            st_tagged(&part[G.item * PART_WORDS + 2 * HD + h], tp, __float_as_uint(M));
+            st_tagged(&part[G.item * PART_WORDS + 2 * HD + 2 + h], tp, __float_as_uint(L));
+        }
     }
     const int j0 = split_lo(2 * HD, G.S, G.s), j1 = split_lo(2 * HD, G.S, G.s + 1);
     const int j = j0 + cs.tid;

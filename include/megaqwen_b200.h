@@ -93,6 +93,38 @@ int launch_a10_int8_decode(
     int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
     const ScalePointers* scales, cudaStream_t stream);
 
+/*
+ * Allocation-free INT8 decode step.  No counterpart in the reference: it is an
+ * addition for callers that cannot call cudaMalloc when they decode -- a plugin
+ * whose host framework owns all device memory through a pre-sized arena, or a
+ * process that locks its allocator after start-up.  launch_a10_int8_decode
+ * allocates its hand-off workspace on the first call on a device; this entry
+ * point instead uses a workspace in a static device array of the library
+ * (about 0.8 MB per GPU that loads the library, held until process exit) and
+ * never calls cudaMalloc, cudaFree or any allocating routine.
+ *   - Same arguments and results as launch_a10_int8_decode, without the scratch
+ *     pointers the kernel does not use (hidden_buffer .. g_mlp_intermediate,
+ *     block_max_vals, block_max_idxs).
+ *   - Limit: num_layers <= 32 (MQ_ERR_SIZE otherwise); up to 18 attention
+ *     splits per KV head, which covers every position < max_seq_len.
+ *   - The first call on a device does a one-time set-up (it looks up the
+ *     device address of the static array and sets the kernel's shared-memory
+ *     attribute); make that first call before any stream capture.
+ *   - All calls on a device share the one array, which keeps the previous
+ *     call's contents (the call clears the error word itself).  Calls that
+ *     overlap on the GPU -- e.g. issued on two streams without ordering --
+ *     race on it: serialise them.
+ *   - A device-side failure (a bounded wait that ran out) is reported by
+ *     *output_token_id == -1.
+ */
+int launch_a10_int8_decode_static(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale,
+    const void* cos_table, const void* sin_table, void* k_cache, void* v_cache, void* g_normalized,
+    int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
+    const ScalePointers* scales, cudaStream_t stream);
+
 /* BF16 fused decode step.  Replaces launch_a10_decode
  * (a10_decode_kernel.cu:761-780): same arguments as the INT8 entry point minus
  * lm_head_scale and scales; weights are bf16. */

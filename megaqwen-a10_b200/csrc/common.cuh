@@ -31,6 +31,7 @@ constexpr int STAGE_BYTES = 16384;
 constexpr int NSTAGE = 10;
 constexpr int KV_CHUNK_POS = STAGE_BYTES / (2 * HD * 2);  // 32 positions of K then V
 constexpr int MAX_SPLITS = 18;                // attention splits per KV head
+constexpr int MAX_DEV_STATIC = 64;            // devices tracked by the allocation-free entry point
 constexpr int MAX_LAYERS = 32;                // pointer/scale tables staged in shared memory
 constexpr int MIN_CTAS = 148;                 // row shares below assume >= 148 CTAs (B200)
 constexpr int QKV_MAXR = (QKV_ROWS + MIN_CTAS - 1) / MIN_CTAS;   // 28 rows per CTA

@@ -1260,3 +1260,92 @@ extern "C" int mqdbg_set_stamp_buffer(unsigned long long* buf) {
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_dbg_n, &zero, sizeof(zero));
     return (int)e;
 }
+
+// ===========================================================================
+// Allocation-free INT8 decode step.
+//
+// Some callers cannot call cudaMalloc at the point where they decode: a plugin
+// running inside a host framework that owns all device memory through its own
+// pre-sized arena, a process whose allocator is locked after start-up, or code
+// that must not allocate between the set-up and the serving loop.  For them the
+// hand-off workspace of the decode kernel lives in the static device array
+// below instead of in the lazily cudaMalloc'd one.  Every GPU that loads this
+// library keeps these bytes resident until the process exits.
+//
+// Limit: the array holds exactly one Workspace (sizeof(mq::Workspace), about
+// 0.8 MB), which serves models of up to MAX_LAYERS (32) layers and up to
+// MAX_SPLITS (18) attention splits per KV head; num_layers above the limit is
+// rejected with MQ_ERR_SIZE.
+// ===========================================================================
+static __device__ __align__(256) unsigned char g_static_workspace[sizeof(mq::Workspace)];
+
+namespace {
+struct StaticDevState {
+    mq::Workspace* ws = nullptr;   // device address of g_static_workspace on this device
+    int num_sms = 0;
+    bool attr_set = false;
+    unsigned long long launches = 0;
+};
+StaticDevState g_static_dev[mq::MAX_DEV_STATIC];
+}  // namespace
+
+extern "C" int launch_a10_int8_decode_static(
+    int input_token_id, int* output_token_id, const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale, const void* cos_table,
+    const void* sin_table, void* k_cache, void* v_cache, void* g_normalized, int num_layers, int position,
+    int cache_len, int max_seq_len, float attn_scale, const ScalePointers* scales, cudaStream_t stream) {
+    int rc = check_common(embed_weight, layer_weights, final_norm_weight, lm_head_weight, cos_table, sin_table,
+                          k_cache, v_cache, num_layers, position, max_seq_len);
+    if (rc) return rc;
+    if (!output_token_id || !lm_head_scale || !scales) return MQ_ERR_ARG;
+    if (cache_len != position + 1) return MQ_ERR_POSITION;
+    if (input_token_id < 0 || input_token_id >= VOCAB) return MQ_ERR_TOKEN;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= MAX_DEV_STATIC) return MQ_ERR_DEVICE;
+    StaticDevState& d = g_static_dev[dev];
+    if (!d.ws) {
+        // One-time set-up on this device (the device is current here): look up
+        // the device address of the static array.  The name itself is only a
+        // host-side stand-in and must never be handed to a kernel.
+        void* ptr = nullptr;
+        if ((e = cudaGetSymbolAddress(&ptr, g_static_workspace)) != cudaSuccess) return (int)e;
+        int sms = 0;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return (int)e;
+        if (sms < MIN_CTAS) return MQ_ERR_DEVICE;
+        d.ws = reinterpret_cast<Workspace*>(ptr);
+        d.num_sms = sms;
+    }
+    if (!d.attr_set) {
+        if ((e = cudaFuncSetAttribute(decode_kernel<W8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sizeof(Smem))) != cudaSuccess)
+            return (int)e;
+        d.attr_set = true;
+    }
+    // The array keeps the previous call's contents.  Tags, counters and the
+    // argmax slot are self-resetting; the error word must start at zero, and
+    // the tagged buffers are cleared before their 32-bit epochs could wrap.
+    const unsigned long long per_launch = (unsigned long long)(num_layers + 1) * TAGS_PER_LAYER;
+    if ((d.launches + 1) * per_launch > 0xF0000000ull) {
+        if ((e = cudaMemsetAsync(d.ws, 0, sizeof(Workspace), stream)) != cudaSuccess) return (int)e;
+        d.launches = 0;
+    }
+    if ((e = cudaMemsetAsync(&d.ws->err_code, 0, 2 * sizeof(int), stream)) != cudaSuccess) return (int)e;
+    d.launches++;
+    DecodeParams P{};
+    P.embed = embed_weight; P.layers = layer_weights; P.scales = scales; P.final_norm = final_norm_weight;
+    P.lm_w = lm_head_weight; P.lm_scale = lm_head_scale;
+    P.cos_t = (const __nv_bfloat16*)cos_table; P.sin_t = (const __nv_bfloat16*)sin_table;
+    P.kc = (__nv_bfloat16*)k_cache; P.vc = (__nv_bfloat16*)v_cache;
+    P.g_normalized = (float*)g_normalized; P.token_out = output_token_id;
+    P.token_in = input_token_id; P.L = num_layers; P.position = position; P.max_seq = max_seq_len;
+    P.attn_scale = attn_scale;
+    P.ws = d.ws;
+    P.budget_ns = g_budget_ns;
+    P.skip_cta = -1;
+    P.splits = choose_splits(position + 1, d.num_sms);
+    void* args[] = {&P};
+    return (int)cudaLaunchCooperativeKernel((const void*)decode_kernel<W8>, dim3(d.num_sms), dim3(NTHREADS), args,
+                                            sizeof(Smem), stream);
+}

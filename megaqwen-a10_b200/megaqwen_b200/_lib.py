@@ -22,7 +22,7 @@ MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 
 EXPORTED = (
     "launch_a10_int8_decode", "launch_a10_decode", "mq_decode_multi", "mq_quantize_per_channel",
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
-    "mq_set_trace",
+    "mq_set_trace", "launch_a10_int8_decode_static",
 )
 
 
@@ -67,6 +67,7 @@ def load():
     lib.mq_set_wait_budget_ns.argtypes = [_u64]
     lib.mq_inject_skip_publish.argtypes = [_i, _i]
     lib.mq_set_trace.argtypes = [_vp, _i]
+    lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]
     lib.mq_kernel_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
     for name in EXPORTED:
         getattr(lib, name).restype = _i

@@ -24,12 +24,21 @@ constexpr int QKV_ROWS = QSZ + 2 * KVSZ;  // 4096
 constexpr int VOCAB = 151936;
 constexpr float RMS_EPS = 1e-6f;
 
-constexpr int NCW = 12;                       // consumer warps
+#ifndef MQ_NCW
+#define MQ_NCW 12
+#endif
+#ifndef MQ_STAGE_BYTES
+#define MQ_STAGE_BYTES 16384
+#endif
+#ifndef MQ_NSTAGE
+#define MQ_NSTAGE 10
+#endif
+constexpr int NCW = MQ_NCW;                   // consumer warps
 constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
-constexpr int STAGE_BYTES = 16384;
-constexpr int NSTAGE = 10;
-constexpr int KV_CHUNK_POS = STAGE_BYTES / (2 * HD * 2);  // 32 positions of K then V
+constexpr int STAGE_BYTES = MQ_STAGE_BYTES;   // ring stage (bulk copy) size
+constexpr int NSTAGE = MQ_NSTAGE;             // ring depth
+constexpr int KV_CHUNK_POS = (STAGE_BYTES / (2 * HD * 2)) < 32 ? (STAGE_BYTES / (2 * HD * 2)) : 32;  // positions of K then V per chunk
 constexpr int MAX_SPLITS = 18;                // attention splits per KV head
 constexpr int MAX_DEV_STATIC = 64;            // devices tracked by the allocation-free entry point
 constexpr int MAX_LAYERS = 32;                // pointer/scale tables staged in shared memory

@@ -58,6 +58,10 @@ enum { TR_START = 0, TR_QKV = 1, TR_ATTN = 2, TR_OIN = 3, TR_O = 4, TR_NORM2 = 5
        TR_DOWN = 8, TRACE_PER_LAYER = 10 };
 
 // Shared-memory layout (dynamic).
+static_assert(NCW <= 12, "attention merge uses x[NCW][2][HD] as scratch");
+static_assert(NCT >= 2 * HD, "attention merge: one consumer thread per (GQA head, dim)");
+static_assert(KV_CHUNK_POS <= 32, "");
+static_assert(STAGE_BYTES >= 2 * INTER && STAGE_BYTES >= 4 * HIDDEN, "a stage must hold one bf16 down row and one bf16 gate+up pair");
 struct Smem {
     uint8_t ring[NSTAGE][STAGE_BYTES];
     uint64_t full[NSTAGE];
@@ -72,8 +76,11 @@ struct Smem {
     float raw[4 * HD];       // raw q0 q1 k v of this CTA's KV head
     float q[2][HD];
     float m[2], l[2], corr[2];
-    float sc[2][KV_CHUNK_POS];
-    float pe[2][KV_CHUNK_POS];
+    float sc[2][32];         // per-warp softmax state during the attention merge
+    float pe[2][32];
+    float ew[2][32];         // merge weights exp(m_w - M_h)
+    float lw_[2][32];        // l_w * ew
+    float mx[2];
     uint16_t kvcur[2][HD];   // current-position K and V, bf16
     unsigned long long best[NCW];
     const void* lw[MAX_LAYERS][11];      // LayerWeights of every layer

@@ -161,6 +161,9 @@ def main():
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-sample-steps", type=int, default=3)
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="profiling case: 100 untimed steps, then 2 steps (capture with ncu -s 100 -c 1)")
+    ap.add_argument("--trace", action="store_true", help="print the per-phase timeline of one step at position 100")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -181,6 +184,18 @@ def main():
     args.warmup = max(args.warmup, 3)
     torch.cuda.set_device(local)
     from megaqwen_b200 import _lib
+    if args.ncu_case or args.trace:
+        dec = build_decoder(args.layers, 256)
+        dec.decode_steps(5, 100)
+        torch.cuda.synchronize()
+        if args.trace:
+            from megaqwen_b200 import trace
+            print(json.dumps(trace.summarize(trace.capture_step(dec), args.layers)))
+        else:
+            dec.decode_steps(5, 2)
+            torch.cuda.synchronize()
+        dec.check_device()
+        return
     K, W, L = args.steps, args.warmup, args.layers
     max_seq = max(K, W, 200) + 8
     dec = build_decoder(L, max_seq)

@@ -21,6 +21,13 @@
 #include "decode.cuh"
 #include <stdlib.h>
 
+// MQ_PHASE_NOINLINE=1 keeps the phase bodies out of line (smaller kernel code).
+#if defined(MQ_PHASE_NOINLINE) && MQ_PHASE_NOINLINE
+#define MQ_PHASE __device__ __noinline__
+#else
+#define MQ_PHASE __device__ __forceinline__
+#endif
+
 // MQ_DEBUG_STAMPS (development aid, off by default): consumer thread 0 of CTA 1
 // appends (id, clock64) pairs to a buffer set with mqdbg_set_stamp_buffer.
 #ifndef MQ_DEBUG_STAMPS
@@ -291,7 +298,7 @@ struct Cons {
 // elements of its fixed 16-byte units in registers for the whole phase.
 // Builds the limbs of x_s[0..n) into shared memory (all consumer threads; the
 // caller guarantees x_s is complete).  Two consumer barriers.
-__device__ __forceinline__ void build_limbs(Cons& cs, const float* x_s, int n) {
+MQ_PHASE void build_limbs(Cons& cs, const float* x_s, int n) {
     Smem* sm = cs.sm;
     float m = 0.f;
     for (int i = cs.tid; i < n; i += NCT) m = fmaxf(m, fabsf(x_s[i]));
@@ -316,7 +323,7 @@ __device__ __forceinline__ void build_limbs(Cons& cs, const float* x_s, int n) {
 }
 
 template <class WT, int K, class Scl, class Out>
-__device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
+MQ_PHASE void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
@@ -368,7 +375,7 @@ __device__ __forceinline__ void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const
 
 // gate/up pair phase: out(i, gate_dot, up_dot).
 template <class WT, class Out>
-__device__ __forceinline__ void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const float* sg,
+MQ_PHASE void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const float* sg,
                                          const float* su, Out out) {
     constexpr int K = HIDDEN;
     constexpr int ESZ = Bytes<WT>::ESZ;
@@ -447,7 +454,7 @@ struct NormW {  // one thread's share of a 1024-wide bf16 norm weight, loaded ah
 // RMSNorm of src[1024] (fp32, smem) -> dst (smem) over the consumer threads:
 // x * rsqrt(mean(x^2) + eps) * w  (int8_decoder.py:228-232).  The weight is
 // already in registers (NormW), so no global load sits on the critical path.
-__device__ __forceinline__ void rmsnorm_1024(Cons& cs, const float* src, const NormW& w, float* dst) {
+MQ_PHASE void rmsnorm_1024(Cons& cs, const float* src, const NormW& w, float* dst) {
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < NORM_PER; ++k) {
@@ -555,7 +562,7 @@ __device__ __forceinline__ void qk_norm_rope(const float* raw, const RopeRegs& R
     }
 }
 
-__device__ void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo& G, int l, uint32_t epoch) {
+MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo& G, int l, uint32_t epoch) {
     Smem* sm = cs.sm;
     const int par = l & 1;
     const uint32_t tq = tag_of(epoch, l, E_QKV);

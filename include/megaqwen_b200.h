@@ -144,20 +144,27 @@ int launch_a10_decode(
  * Multi-step decode with on-device token feedback (no reference counterpart:
  * the reference runs one launch plus one .item() per token,
  * bench_int8.py:193-219).  Runs `num_steps` greedy steps starting at
- * `position`; the first input token is *d_token_in (device int32), each later
- * input is the previous step's argmax.  Token j is written to d_tokens_out[j].
+ * `position`; the first input token is *d_token_in (device int32) or, when
+ * d_token_in is NULL, `input_token`; each later input is the previous step's
+ * argmax.  Token j is written to d_tokens_out[j] (device int32).
  * weight_kind: 0 = INT8 (lm_head_scale and scales required), 1 = BF16.
+ * row_pad_bytes: 0 when every weight matrix (the seven projections and the LM
+ *   head) is dense row-major [out, in] as the reference stores it; 16 when each
+ *   row is followed by 16 padding bytes (row stride = row bytes + 16).  The
+ *   padded layout lets the kernel stream several rows with one bulk copy; the
+ *   Python decoder classes repack into it once at construction.
  * d_logits (optional, may be NULL): fp32[151936] logits of the LAST step.
  * d_layer_hidden (optional, may be NULL): fp32[num_layers][1024], the bf16
  *   residual stream after each layer of the LAST step (diagnostics/parity).
  */
 int mq_decode_multi(
-    int weight_kind, const int* d_token_in, int* d_tokens_out, int num_steps,
+    int weight_kind, int input_token, const int* d_token_in, int* d_tokens_out, int num_steps,
     const void* embed_weight, const LayerWeights* layer_weights,
     const void* final_norm_weight, const void* lm_head_weight, const float* lm_head_scale,
     const ScalePointers* scales, const void* cos_table, const void* sin_table,
     void* k_cache, void* v_cache, float* g_normalized, float* d_logits, float* d_layer_hidden,
-    int num_layers, int position, int max_seq_len, float attn_scale, cudaStream_t stream);
+    int num_layers, int position, int max_seq_len, float attn_scale, int row_pad_bytes,
+    cudaStream_t stream);
 
 /*
  * Per-output-channel symmetric INT8 quantizer.  Same arithmetic as

@@ -28,7 +28,7 @@ constexpr float RMS_EPS = 1e-6f;
 #define MQ_NCW 12
 #endif
 #ifndef MQ_STAGE_BYTES
-#define MQ_STAGE_BYTES 16384
+#define MQ_STAGE_BYTES 16640
 #endif
 #ifndef MQ_NSTAGE
 #define MQ_NSTAGE 10
@@ -38,7 +38,12 @@ constexpr int NCT = NCW * 32;                 // consumer threads
 constexpr int NTHREADS = NCT + 32;            // + producer warp
 constexpr int STAGE_BYTES = MQ_STAGE_BYTES;   // ring stage (bulk copy) size
 constexpr int NSTAGE = MQ_NSTAGE;             // ring depth
+// Weight rows are placed in the ring at a stride of (row bytes + ROW_SKEW): the
+// 16-byte skew puts consecutive rows in different shared-memory bank groups, so
+// ldmatrix over 8 rows is conflict-free.  16 int8 rows of 1024 fill a stage.
+constexpr int ROW_SKEW = 16;
 constexpr int KV_CHUNK_POS = (STAGE_BYTES / (2 * HD * 2)) < 32 ? (STAGE_BYTES / (2 * HD * 2)) : 32;  // positions of K then V per chunk
+constexpr int KV_V_OFFSET = KV_CHUNK_POS * HD * 2;  // V rows follow the K rows in a chunk
 constexpr int MAX_SPLITS = 18;                // attention splits per KV head
 constexpr int MAX_DEV_STATIC = 64;            // devices tracked by the allocation-free entry point
 constexpr int MAX_LAYERS = 32;                // pointer/scale tables staged in shared memory

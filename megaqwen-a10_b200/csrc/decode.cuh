@@ -51,6 +51,7 @@ struct DecodeParams {
     int skip_cta;                   // test hook: CTA that skips its layer-0 QKV publish (-1: none)
     unsigned long long* trace;      // optional [gridDim.x][trace_slots] globaltimer stamps
     int trace_slots;
+    int row_pad;                    // 0: weight rows dense (reference layout); ROW_SKEW: rows padded to rb + ROW_SKEW
 };
 
 // Trace slots: per layer l, stamps at l * TRACE_PER_LAYER + event.
@@ -61,7 +62,9 @@ enum { TR_START = 0, TR_QKV = 1, TR_ATTN = 2, TR_OIN = 3, TR_O = 4, TR_NORM2 = 5
 static_assert(NCW <= 12, "attention merge uses x[NCW][2][HD] as scratch");
 static_assert(NCT >= 2 * HD, "attention merge: one consumer thread per (GQA head, dim)");
 static_assert(KV_CHUNK_POS <= 32, "");
-static_assert(STAGE_BYTES >= 2 * INTER && STAGE_BYTES >= 4 * HIDDEN, "a stage must hold one bf16 down row and one bf16 gate+up pair");
+static_assert(STAGE_BYTES >= 2 * INTER + ROW_SKEW && STAGE_BYTES >= 2 * (2 * HIDDEN + ROW_SKEW),
+              "a stage must hold one bf16 down row and one bf16 gate+up pair");
+static_assert(STAGE_BYTES >= 16 * (HIDDEN + ROW_SKEW), "16 int8 rows of 1024 per stage (one mma tile)");
 struct Smem {
     uint8_t ring[NSTAGE][STAGE_BYTES];
     uint64_t full[NSTAGE];
@@ -72,7 +75,7 @@ struct Smem {
     float red[NCW];
     float red2[NCW];
     float limb_inv;
-    alignas(16) int limb[3][INTER / 4];  // activation limbs of the current matvec phase (int4 loads)
+    alignas(16) int limb[4][INTER / 4];  // activation limbs of the current matvec phase; row 3 stays zero
     float raw[4 * HD];       // raw q0 q1 k v of this CTA's KV head
     float q[2][HD];
     float m[2], l[2], corr[2];

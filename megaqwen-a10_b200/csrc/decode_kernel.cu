@@ -30,6 +30,10 @@
 
 // MQ_DEBUG_STAMPS (development aid, off by default): consumer thread 0 of CTA 1
 // appends (id, clock64) pairs to a buffer set with mqdbg_set_stamp_buffer.
+// MQ_NO_STREAM (timing experiment only, wrong results): no weight streaming.
+#ifndef MQ_NO_STREAM
+#define MQ_NO_STREAM 0
+#endif
 #ifndef MQ_DEBUG_STAMPS
 #define MQ_DEBUG_STAMPS 0
 #endif
@@ -175,6 +179,20 @@ struct Bytes {
 struct Producer {
     Smem* sm;
     uint32_t seq;
+    int pad;  // global row padding: 0 (dense rows, one copy per row) or ROW_SKEW (one copy per run)
+
+    // Copies rows [a, b) of a matrix with rb payload bytes per row into dst at a
+    // stride of rb + ROW_SKEW.  With padded rows the global layout already has
+    // that stride and the run is one bulk copy.
+    __device__ void run(uint8_t* dst, const uint8_t* base, int a, int n, int rb, uint64_t* bar) {
+        const int rs = rb + ROW_SKEW;
+        if (pad) {
+            bulk_g2s(dst, base + (size_t)a * rs, n * rs, bar);
+        } else {
+            for (int i = 0; i < n; ++i) bulk_g2s(dst + i * rs, base + (size_t)(a + i) * rb, rb, bar);
+        }
+    }
+    __device__ uint32_t bytes(int n, int rb) const { return pad ? n * (rb + ROW_SKEW) : n * rb; }
 
     __device__ bool begin(Ctx& c, uint32_t bytes, uint8_t*& dst) {
         const uint32_t stage = seq % NSTAGE, use = seq / NSTAGE;
@@ -185,14 +203,15 @@ struct Producer {
     }
     __device__ void end() { ++seq; }
 
-    // rows [a, b) of a row-major matrix with `rb` bytes per row.
+    // rows [a, b) of a row-major matrix with `rb` bytes per row, placed in the
+    // stage at a stride of rb + ROW_SKEW (one bulk copy per row).
     __device__ bool rows(Ctx& c, const uint8_t* base, int a, int b, int rb) {
-        const int rpc = STAGE_BYTES / rb;
+        const int rs = rb + ROW_SKEW, rpc = STAGE_BYTES / rs;
         for (int r = a; r < b; r += rpc) {
             const int n = min(rpc, b - r);
             uint8_t* dst;
-            if (!begin(c, n * rb, dst)) return false;
-            bulk_g2s(dst, base + (size_t)r * rb, n * rb, &sm->full[seq % NSTAGE]);
+            if (!begin(c, bytes(n, rb), dst)) return false;
+            run(dst, base, r, n, rb, &sm->full[seq % NSTAGE]);
             end();
         }
         return true;
@@ -202,28 +221,28 @@ struct Producer {
 template <class WT>
 __device__ void producer_main(const DecodeParams& P, Ctx& c, const Geo& G) {
     constexpr int ESZ = Bytes<WT>::ESZ;
-    Producer pr{c.sm, 0};
+    Producer pr{c.sm, 0, P.row_pad};
     bool ok = true;
     for (int l = 0; l < P.L && ok; ++l) {
         const LayerWeights& w = P.layers[l];
         // QKV rows in the stacked [q; k; v] row space.
         {
-            const int rb = HIDDEN * ESZ, rpc = STAGE_BYTES / rb;
+            const int rb = HIDDEN * ESZ, rs = rb + ROW_SKEW, rpc = STAGE_BYTES / rs;
             for (int r = G.qkv0; r < G.qkv1 && ok; r += rpc) {
                 const int n = min(rpc, G.qkv1 - r);
                 uint8_t* dst;
-                if (!(ok = pr.begin(c, n * rb, dst))) break;
+                if (!(ok = pr.begin(c, pr.bytes(n, rb), dst))) break;
                 uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
                 int done = 0;
-                while (done < n) {
+                while (done < n) {  // runs within the q, k and v matrices
                     const int row = r + done;
-                    const uint8_t* src;
-                    int lim;
-                    if (row < QSZ) { src = (const uint8_t*)w.q_proj_weight + (size_t)row * rb; lim = QSZ; }
-                    else if (row < QSZ + KVSZ) { src = (const uint8_t*)w.k_proj_weight + (size_t)(row - QSZ) * rb; lim = QSZ + KVSZ; }
-                    else { src = (const uint8_t*)w.v_proj_weight + (size_t)(row - QSZ - KVSZ) * rb; lim = QKV_ROWS; }
+                    const uint8_t* base;
+                    int first, lim;
+                    if (row < QSZ) { base = (const uint8_t*)w.q_proj_weight; first = 0; lim = QSZ; }
+                    else if (row < QSZ + KVSZ) { base = (const uint8_t*)w.k_proj_weight; first = QSZ; lim = QSZ + KVSZ; }
+                    else { base = (const uint8_t*)w.v_proj_weight; first = QSZ + KVSZ; lim = QKV_ROWS; }
                     const int m = min(n - done, lim - row);
-                    bulk_g2s(dst + done * rb, src, m * rb, bar);
+                    pr.run(dst + done * rs, base, row - first, m, rb, bar);
                     done += m;
                 }
                 pr.end();
@@ -238,21 +257,21 @@ __device__ void producer_main(const DecodeParams& P, Ctx& c, const Geo& G) {
                 if (!(ok = pr.begin(c, 2 * n * HD * 2, dst))) break;
                 uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
                 bulk_g2s(dst, P.kc + head_off + (size_t)p * HD, n * HD * 2, bar);
-                bulk_g2s(dst + KV_CHUNK_POS * HD * 2, P.vc + head_off + (size_t)p * HD, n * HD * 2, bar);
+                bulk_g2s(dst + KV_V_OFFSET, P.vc + head_off + (size_t)p * HD, n * HD * 2, bar);
                 pr.end();
             }
         }
         if (ok) ok = pr.rows(c, (const uint8_t*)w.o_proj_weight, G.o0, G.o1, QSZ * ESZ);
         // gate/up: a chunk holds n gate rows followed by the same n up rows.
         if (ok) {
-            const int rb = HIDDEN * ESZ, rpc = STAGE_BYTES / (2 * rb);
+            const int rb = HIDDEN * ESZ, rs = rb + ROW_SKEW, rpc = STAGE_BYTES / (2 * rs);
             for (int r = G.gu0; r < G.gu1 && ok; r += rpc) {
                 const int n = min(rpc, G.gu1 - r);
                 uint8_t* dst;
-                if (!(ok = pr.begin(c, 2 * n * rb, dst))) break;
+                if (!(ok = pr.begin(c, 2 * pr.bytes(n, rb), dst))) break;
                 uint64_t* bar = &c.sm->full[pr.seq % NSTAGE];
-                bulk_g2s(dst, (const uint8_t*)w.gate_proj_weight + (size_t)r * rb, n * rb, bar);
-                bulk_g2s(dst + n * rb, (const uint8_t*)w.up_proj_weight + (size_t)r * rb, n * rb, bar);
+                pr.run(dst, (const uint8_t*)w.gate_proj_weight, r, n, rb, bar);
+                pr.run(dst + n * rs, (const uint8_t*)w.up_proj_weight, r, n, rb, bar);
                 pr.end();
             }
         }
@@ -282,6 +301,9 @@ struct Cons {
     __device__ const uint8_t* wait(Ctx& c, int where) {
         const uint32_t stage = seq % NSTAGE;
         dbg(100 + where);
+#if MQ_NO_STREAM
+        return sm->ring[stage];
+#endif
         mbar_wait(c, &sm->full[stage], (seq / NSTAGE) & 1, where);
         dbg(200 + where);
         return sm->ring[stage];
@@ -290,6 +312,19 @@ struct Cons {
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->empty[seq % NSTAGE]);
         ++seq;
+    }
+    // The q-th chunk after the next one (q = 0 is what wait() would return).
+    __device__ const uint8_t* wait_at(Ctx& c, uint32_t q, int where) {
+        const uint32_t s = seq + q, stage = s % NSTAGE;
+        mbar_wait(c, &sm->full[stage], (s / NSTAGE) & 1, where);
+        return sm->ring[stage];
+    }
+    // Releases the next n chunks (after wait_at on each of them).
+    __device__ void release_n(uint32_t n) {
+        __syncwarp();
+        if (lane == 0)
+            for (uint32_t q = 0; q < n; ++q) mbar_arrive(&sm->empty[(seq + q) % NSTAGE]);
+        seq += n;
     }
 };
 
@@ -316,7 +351,7 @@ MQ_PHASE void build_limbs(Cons& cs, const float* x_s, int n) {
         limb_split(v.y, up, p0, p1, p2, 1);
         limb_split(v.z, up, p0, p1, p2, 2);
         limb_split(v.w, up, p0, p1, p2, 3);
-        sm->limb[0][w] = (int)p0; sm->limb[1][w] = (int)p1; sm->limb[2][w] = (int)p2;
+        sm->limb[0][w] = (int)p0; sm->limb[1][w] = (int)p1; sm->limb[2][w] = (int)p2; sm->limb[3][w] = 0;
     }
     if (cs.tid == 0) sm->limb_inv = inv;
     consumers_sync();
@@ -327,7 +362,8 @@ MQ_PHASE void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl s
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
-    constexpr int RPC = STAGE_BYTES / RB;
+    constexpr int RS = RB + ROW_SKEW;
+    constexpr int RPC = STAGE_BYTES / RS;
     float xr[WT::LIMBS ? 1 : UPL * WT::EPU];
     Limbs<WT::LIMBS ? UPL * 4 : 4> lb;
     if constexpr (WT::LIMBS) {
@@ -352,7 +388,7 @@ MQ_PHASE void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl s
         int i = cb + ((cs.warp - cb) % NCW + NCW) % NCW;
         for (; i < ce; i += NCW) {
             const float sc = scl(r0 + i);
-            const uint4* row = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
+            const uint4* row = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RS);
             float part;
             if constexpr (WT::LIMBS) {
                 int a0 = 0, a1 = 0, a2 = 0;
@@ -381,7 +417,8 @@ MQ_PHASE void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const
     constexpr int ESZ = Bytes<WT>::ESZ;
     constexpr int RB = K * ESZ;
     constexpr int UPL = K / (WT::EPU * 32);
-    constexpr int RPC = STAGE_BYTES / (2 * RB);
+    constexpr int RS = RB + ROW_SKEW;
+    constexpr int RPC = STAGE_BYTES / (2 * RS);
     float xr[WT::LIMBS ? 1 : UPL * WT::EPU];
     Limbs<WT::LIMBS ? UPL * 4 : 4> lb;
     if constexpr (WT::LIMBS) {
@@ -408,8 +445,8 @@ MQ_PHASE void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const
         for (; i < ce; i += NCW) {
             float gsc = 1.f, usc = 1.f;
             if (WT::HAS_SCALE) { gsc = sg[i]; usc = su[i]; }  // phase-relative, shared memory
-            const uint4* grow = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RB);
-            const uint4* urow = reinterpret_cast<const uint4*>(st + (size_t)(nin + i - cb) * RB);
+            const uint4* grow = reinterpret_cast<const uint4*>(st + (size_t)(i - cb) * RS);
+            const uint4* urow = reinterpret_cast<const uint4*>(st + (size_t)(nin + i - cb) * RS);
             float gp, up;
             if constexpr (WT::LIMBS) {
                 int g0 = 0, g1 = 0, g2 = 0, u0 = 0, u1 = 0, u2 = 0;
@@ -433,6 +470,88 @@ MQ_PHASE void gu_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, const
             const float gd = warp_sum(gp);
             const float ud = warp_sum(up);
             if (cs.lane == 0) out(r0 + i, gd * gsc, ud * usc);
+        }
+        cs.release();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// INT8 matvec on the tensor cores for the throughput-bound LM head (and the
+// stand-alone mq_matvec), exact: mma.sync m16n8k32 s8 x s8 -> s32 with
+// A = 16 weight rows x 32 bytes (ldmatrix from the skewed ring rows) and
+// B = the activation limbs (column n of B = limb n for n < 3, zero otherwise).
+// The int32 results are the same exact integers the dp4a formulation yields.
+// The latency-bound per-layer phases use the dp4a path (mv_phase / gu_phase):
+// a dependent mma.sync chain of a few steps is slower there.
+// ---------------------------------------------------------------------------
+// st[q] for a runtime q without dynamic register-array indexing.
+template <int N>
+__device__ __forceinline__ const uint8_t* pick(const uint8_t* const (&st)[N], int q) {
+    const uint8_t* r = st[0];
+#pragma unroll
+    for (int k = 1; k < N; ++k) r = (q == k) ? st[k] : r;
+    return r;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// This lane's ldmatrix row address for tile row tr (lanes 0-7: rows 0-7 bytes
+// 0-15, 8-15: rows 8-15 bytes 0-15, 16-23: rows 0-7 bytes 16-31, 24-31: rows 8-15).
+__device__ __forceinline__ int mma_lane_row(int lane) { return (lane & 7) + 8 * ((lane >> 3) & 1); }
+__device__ __forceinline__ int mma_lane_koff(int lane) { return 16 * (lane >> 4); }
+
+__device__ __forceinline__ float limb_finish(long long a0, long long a1, long long a2, float inv) {
+    const double v = fma((double)a2, 65536.0, fma((double)a1, 256.0, (double)a0));
+    return (float)v * inv;
+}
+
+// Streaming phase (LM head, stand-alone matvec): every ring chunk is one tile
+// (<= 16 rows) done by one warp (chunk q -> warp q % NCW) over all k-steps.
+// out(row, value) is called by lanes t == 0 (two rows each).
+template <int K, class Scl, class Out>
+__device__ __forceinline__ void mma_stream(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
+    constexpr int RS = K + ROW_SKEW;
+    constexpr int RPC = STAGE_BYTES / RS;
+    constexpr int KS = K / 32;
+    static_assert(RPC <= 16, "one tile per chunk");
+    build_limbs(cs, x_s, K);
+    const int g = cs.lane >> 2, t = cs.lane & 3;
+    const int* lb = cs.sm->limb[g < 3 ? g : 3];
+    const float inv = cs.sm->limb_inv;
+    const int n = r1 - r0;
+    for (int cb = 0, q = 0; cb < n; cb += RPC, ++q) {
+        const uint8_t* st = cs.wait(c, 1);
+        if (q % NCW == cs.warp) {
+            const int rows = min(RPC, n - cb);
+            const int tr = min(mma_lane_row(cs.lane), rows - 1);
+            const uint32_t abase = smem_u32(st + (size_t)tr * RS) + mma_lane_koff(cs.lane);
+            int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+            for (int ks = 0; ks < KS; ks += 2) {
+                uint32_t a[4], b[4];
+                ldmatrix_x4(a, abase + ks * 32);
+                ldmatrix_x4(b, abase + ks * 32 + 32);
+                mma_s8(d0, a, (uint32_t)lb[8 * ks + t], (uint32_t)lb[8 * ks + 4 + t]);
+                mma_s8(d1, b, (uint32_t)lb[8 * ks + 8 + t], (uint32_t)lb[8 * ks + 12 + t]);
+            }
+            // limb 2 of rows g, g+8 lives in lane t == 1 (column 2)
+            const int x0 = d0[0] + d1[0], x1 = d0[1] + d1[1], x2 = d0[2] + d1[2], x3 = d0[3] + d1[3];
+            const int l2a = __shfl_down_sync(0xffffffffu, x0, 1);
+            const int l2b = __shfl_down_sync(0xffffffffu, x2, 1);
+            if (t == 0) {
+                if (g < rows) out(r0 + cb + g, limb_finish(x0, x1, l2a, inv) * scl(r0 + cb + g));
+                if (g + 8 < rows) out(r0 + cb + g + 8, limb_finish(x2, x3, l2b, inv) * scl(r0 + cb + g + 8));
+            }
         }
         cs.release();
     }
@@ -639,7 +758,7 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         const int n = min(KV_CHUNK_POS, G.past1 - p);
         const uint8_t* st = cs.wait(c, 3);
         const uint16_t* kb = reinterpret_cast<const uint16_t*>(st);
-        const uint16_t* vb = reinterpret_cast<const uint16_t*>(st + KV_CHUNK_POS * HD * 2);
+        const uint16_t* vb = reinterpret_cast<const uint16_t*>(st + KV_V_OFFSET);
         for (int t = ((cs.warp - qi) % NCW + NCW) % NCW; t < n; t += NCW) step(kb + t * HD, vb + t * HD);
         cs.release();
         qi += n;
@@ -800,9 +919,10 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
             const bool skip = (l == 0 && G.b == P.skip_cta);
             uint64_t* dst = ws->xqkv[par];
             auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[r - G.qkv0] : 1.f; };
-            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, scl, [&](int r, float d) {
+            auto out = [&](int r, float d) {
                 if (!skip) st_tagged(&dst[r], t, __float_as_uint(d));
-            });
+            };
+            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_QKV);
         // --- attention (only CTAs that own an item) ---
@@ -821,9 +941,8 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
             const uint32_t t = tag_of(epoch, l, E_ACT);
             uint64_t* dst = ws->xact[par];
             auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_O + r - G.o0] : 1.f; };
-            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, scl, [&](int r, float d) {
-                st_tagged(&dst[r], t, __float_as_uint(d + sm->h[r]));
-            });
+            auto out = [&](int r, float d) { st_tagged(&dst[r], t, __float_as_uint(d + sm->h[r])); };
+            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_O);
         // --- post-attention norm + gate/up ---
@@ -836,10 +955,11 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
         {
             const uint32_t t = tag_of(epoch, l, E_MLP);
             uint64_t* dst = ws->xmlp[par];
-            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, lsc + SCL_G, lsc + SCL_U, [&](int r, float gd, float ud) {
+            auto out = [&](int r, float gd, float ud) {
                 const float silu = gd / (1.0f + expf(-gd));
                 st_tagged(&dst[r], t, __float_as_uint(silu * ud));
-            });
+            };
+            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, lsc + SCL_G, lsc + SCL_U, out);
         }
         trace_stamp(P, cs, tb + TR_GU);
         // --- down + residual -> next h (bf16) ---
@@ -852,9 +972,8 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
             const uint32_t t = tag_of(epoch, l + 1, E_H);
             uint64_t* dst = ws->xh[(l + 1) & 1];
             auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_D + r - G.d0] : 1.f; };
-            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, scl, [&](int r, float d) {
-                st_tagged(&dst[r], t, f32_to_bf16_bits(d + sm->act[r]));
-            });
+            auto out = [&](int r, float d) { st_tagged(&dst[r], t, f32_to_bf16_bits(d + sm->act[r])); };
+            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_DOWN);
     }
@@ -878,10 +997,19 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     {
         float* logits = P.logits;
         auto scl = [&](int r) { return WT::HAS_SCALE ? sm->lm_scl[r - G.lm0] : 1.f; };
-        mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, [&](int r, float d) {
+        auto out = [&](int r, float d) {
             if (logits) logits[r] = d;
-            if (d > best_v) { best_v = d; best_i = r; }
-        });
+            if (d > best_v || (d == best_v && r < best_i)) { best_v = d; best_i = r; }
+        };
+        if constexpr (WT::LIMBS) mma_stream<HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, out);
+        else mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, out);
+    }
+    // argmax over the lanes of the warp (ties: lowest row)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (ov > best_v || (ov == best_v && oi < best_i)) { best_v = ov; best_i = oi; }
     }
     if (cs.lane == 0) {
         sm->best[cs.warp] = best_i == 0x7fffffff ? 0ull
@@ -924,7 +1052,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
     __syncthreads();
     unsigned long long cta_key = 0ull;
     if (threadIdx.x >= NCT) {
+#if !MQ_NO_STREAM
         if (threadIdx.x == NCT) producer_main<WT>(P, c, G);
+#endif
     } else {
         consumer_main<WT>(P, c, G, epoch, token, cta_key);
     }
@@ -972,7 +1102,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) matvec_kernel(const MatvecParams 
     __syncthreads();
     if (threadIdx.x >= NCT) {
         if (threadIdx.x == NCT) {
-            Producer pr{sm, 0};
+            Producer pr{sm, 0, 0};
             pr.rows(c, (const uint8_t*)P.W, r0, r1, K * Bytes<WT>::ESZ);
             const uint32_t first = pr.seq > (uint32_t)NSTAGE ? pr.seq - NSTAGE : 0u;
             for (uint32_t q = first; q < pr.seq; ++q) {
@@ -986,7 +1116,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) matvec_kernel(const MatvecParams 
         const float* sc = P.scale;
         float* y = P.y;
         auto scl = [&](int r) { return WT::HAS_SCALE ? __ldg(sc + r) : 1.f; };
-        mv_phase<WT, K>(c, cs, r0, r1, sm->x, scl, [&](int r, float d) { y[r] = d; });
+        auto out = [&](int r, float d) { y[r] = d; };
+        if constexpr (WT::LIMBS) mma_stream<K>(c, cs, r0, r1, sm->x, scl, out);
+        else mv_phase<WT, K>(c, cs, r0, r1, sm->x, scl, out);
     }
     __syncthreads();
 }
@@ -1151,15 +1283,17 @@ extern "C" int launch_a10_decode(
     return launch_step(1, P, stream);
 }
 
-extern "C" int mq_decode_multi(int weight_kind, const int* d_token_in, int* d_tokens_out, int num_steps,
+extern "C" int mq_decode_multi(int weight_kind, int input_token, const int* d_token_in, int* d_tokens_out, int num_steps,
                                const void* embed_weight, const LayerWeights* layer_weights,
                                const void* final_norm_weight, const void* lm_head_weight,
                                const float* lm_head_scale, const ScalePointers* scales, const void* cos_table,
                                const void* sin_table, void* k_cache, void* v_cache, float* g_normalized,
                                float* d_logits, float* d_layer_hidden, int num_layers, int position,
-                               int max_seq_len, float attn_scale, cudaStream_t stream) {
+                               int max_seq_len, float attn_scale, int row_pad_bytes, cudaStream_t stream) {
     if (weight_kind != 0 && weight_kind != 1) return MQ_ERR_ARG;
-    if (!d_token_in || !d_tokens_out || num_steps <= 0) return MQ_ERR_ARG;
+    if (!d_tokens_out || num_steps <= 0) return MQ_ERR_ARG;
+    if (row_pad_bytes != 0 && row_pad_bytes != ROW_SKEW) return MQ_ERR_ARG;
+    if (!d_token_in && (input_token < 0 || input_token >= VOCAB)) return MQ_ERR_TOKEN;
     int rc = check_common(embed_weight, layer_weights, final_norm_weight, lm_head_weight, cos_table, sin_table,
                           k_cache, v_cache, num_layers, position, max_seq_len);
     if (rc) return rc;
@@ -1176,6 +1310,8 @@ extern "C" int mq_decode_multi(int weight_kind, const int* d_token_in, int* d_to
         P.logits = last ? d_logits : nullptr;
         P.layer_hidden = last ? d_layer_hidden : nullptr;
         P.token_in_dev = j == 0 ? d_token_in : d_tokens_out + (j - 1);
+        P.token_in = input_token;
+        P.row_pad = row_pad_bytes;
         P.token_out = d_tokens_out + j;
         P.L = num_layers; P.position = position + j; P.max_seq = max_seq_len; P.attn_scale = attn_scale;
         if ((rc = launch_step(weight_kind, P, stream))) return rc;

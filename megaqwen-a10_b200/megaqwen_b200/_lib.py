@@ -17,6 +17,7 @@ MQ_ERRORS = {
     -4: "device unsupported",
     -5: "size larger than the entry point supports",
 }
+ROW_PAD = 16  # padding bytes after every weight row in the layout the decoder classes use
 MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 3: "invalid fed-back token"}
 
 EXPORTED = (
@@ -59,8 +60,7 @@ def load():
     ref_args = [_i, _vp, _vp, _vp, _vp, _vp]  # token, out, embed, layers, final_norm, lm_head
     lib.launch_a10_int8_decode.argtypes = ref_args + [_vp, _vp, _vp] + [_vp] * 3 + [_vp] * 10 + [_i, _i, _i, _i, _f, _vp, _vp]
     lib.launch_a10_decode.argtypes = ref_args + [_vp, _vp] + [_vp] * 3 + [_vp] * 10 + [_i, _i, _i, _i, _f, _vp]
-    lib.mq_decode_multi.argtypes = [_i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
-                                    _vp, _i, _i, _i, _f, _vp]
+    lib.mq_decode_multi.argtypes = [_i, _i, _vp, _vp, _i] + [_vp] * 13 + [_i, _i, _i, _f, _i, _vp]
     lib.mq_quantize_per_channel.argtypes = [_vp, _i64, _i64, _vp, _vp, _vp]
     lib.mq_matvec.argtypes = [_i, _vp, _vp, _vp, _vp, _i, _i, _vp]
     lib.mq_device_status.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), _i]

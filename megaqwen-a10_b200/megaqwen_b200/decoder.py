@@ -85,7 +85,18 @@ class _MegakernelDecoderBase:
         for i in range(num_layers):
             for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
                 setattr(arr[i], fname, layer_weights_flat[i * 11 + j].data_ptr())
-        self.d_layer_weights_ = self._to_device_bytes(arr)
+        self.d_layer_weights_ = self._to_device_bytes(arr)  # reference (dense-row) layout
+        # Padded copy of every weight matrix (row stride = row bytes + ROW_PAD): the
+        # kernel then streams a run of rows with one bulk copy.  Built once here.
+        self._pad_keep = []
+        parr = (_lib.LayerWeights * num_layers)()
+        for i in range(num_layers):
+            for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
+                t = layer_weights_flat[i * 11 + j]
+                tp = self._padded(t) if t.dim() == 2 else t
+                setattr(parr[i], fname, tp.data_ptr())
+        self.d_layer_weights_pad_ = self._to_device_bytes(parr)
+        self.lm_head_pad_ = self._padded(lm_head)
         shape = (num_layers, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
         self.k_cache_ = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
         self.v_cache_ = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
@@ -94,6 +105,13 @@ class _MegakernelDecoderBase:
         self.position_ = 0
         self.attn_scale_ = 1.0 / (HEAD_DIM ** 0.5)
         _lib.load()
+
+    def _padded(self, t):
+        extra = _lib.ROW_PAD // t.element_size()
+        p = torch.zeros((t.shape[0], t.shape[1] + extra), dtype=t.dtype, device=t.device)
+        p[:, :t.shape[1]] = t
+        self._pad_keep.append(p)
+        return p
 
     def _to_device_bytes(self, carr):
         host = torch.frombuffer(bytearray(bytes(carr)), dtype=torch.uint8)
@@ -107,10 +125,7 @@ class _MegakernelDecoderBase:
             raise ValueError(f"token {tok} outside [0, {VOCAB_SIZE})")
         if self.position_ >= self.max_seq_len_:
             raise ValueError(f"KV cache full: position {self.position_} >= max_seq_len {self.max_seq_len_}")
-        with torch.cuda.device(self.device):
-            rc = self._launch(tok, torch.cuda.current_stream(self.device).cuda_stream)
-        _lib.check(rc, "decode launch")
-        self.position_ += 1
+        self._run(tok, None, self.output_token_, 1, None, None)
         out = int(self.output_token_.item())
         if out < 0:
             _lib.raise_device_error("decode_step")
@@ -153,18 +168,39 @@ class _MegakernelDecoderBase:
             _check_tensor(logits, "logits", torch.float32, (VOCAB_SIZE,), self.device)
         if layer_hidden is not None:
             _check_tensor(layer_hidden, "layer_hidden", torch.float32, (self.num_layers_, HIDDEN_SIZE), self.device)
+        self._run(0, tok_in, tokens_out, num_steps, logits, layer_hidden)
+        return tokens_out
+
+    def _run(self, tok, tok_dev, tokens_out, num_steps, logits, layer_hidden):
         scale_lm, scales = self._scale_ptrs()
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream(self.device).cuda_stream
             rc = _lib.load().mq_decode_multi(
-                self._kind, _ptr(tok_in), _ptr(tokens_out), int(num_steps), _ptr(self.embed_weight_),
-                _ptr(self.d_layer_weights_), _ptr(self.final_norm_weight_), _ptr(self.lm_head_weight_), scale_lm,
+                self._kind, int(tok), _ptr(tok_dev), _ptr(tokens_out), int(num_steps), _ptr(self.embed_weight_),
+                _ptr(self.d_layer_weights_pad_), _ptr(self.final_norm_weight_), _ptr(self.lm_head_pad_), scale_lm,
                 scales, _ptr(self.cos_table_), _ptr(self.sin_table_), _ptr(self.k_cache_), _ptr(self.v_cache_),
                 _ptr(self.g_normalized_), _ptr(logits), _ptr(layer_hidden), self.num_layers_, self.position_,
-                self.max_seq_len_, ctypes.c_float(self.attn_scale_), ctypes.c_void_p(stream))
+                self.max_seq_len_, ctypes.c_float(self.attn_scale_), _lib.ROW_PAD, ctypes.c_void_p(stream))
         _lib.check(rc, "mq_decode_multi")
         self.position_ += num_steps
-        return tokens_out
+
+    def decode_step_reference_abi(self, input_token_id):
+        """One step through the reference-signature C entry point
+        (launch_a10_int8_decode / launch_a10_decode) on the reference's dense
+        weight layout; same result as decode_step."""
+        tok = int(input_token_id)
+        if not 0 <= tok < VOCAB_SIZE:
+            raise ValueError(f"token {tok} outside [0, {VOCAB_SIZE})")
+        if self.position_ >= self.max_seq_len_:
+            raise ValueError("KV cache full")
+        with torch.cuda.device(self.device):
+            rc = self._launch(tok, torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "decode launch")
+        self.position_ += 1
+        out = int(self.output_token_.item())
+        if out < 0:
+            _lib.raise_device_error("decode_step_reference_abi")
+        return out
 
     def check_device(self):
         """Raises if a previous launch recorded a device-side error."""

@@ -48,7 +48,7 @@ def test_argument_validation_without_gpu():
     assert lib.mq_quantize_per_channel(n, 4, 4, n, n, n) == -1
     assert lib.mq_matvec(0, n, n, n, n, 4, 1024, n) == -1
     assert lib.mq_set_wait_budget_ns(0) == -1
-    assert lib.mq_decode_multi(2, n, n, 1, *([n] * 13), 28, 0, 2048, ctypes.c_float(0.1), n) == -1
+    assert lib.mq_decode_multi(2, 0, n, n, 1, *([n] * 13), 28, 0, 2048, ctypes.c_float(0.1), 16, n) == -1
 
 
 def test_check_raises_on_error_codes():

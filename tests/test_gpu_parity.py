@@ -148,6 +148,16 @@ def test_decode_step_reference_surface(small_state):
         t_o = orc.decode_step(t_o)
     assert dec.position() == 10
     first = dec.decode_step(t_g)
+    # the reference-signature C entry point on the dense layout gives the same step
+    dec.reset()
+    orc2 = O.OracleDecoder(small_state, L, max_seq_len=64)
+    t_in, agree = 5, 0
+    for _ in range(6):   # teacher-forced on the oracle's tokens
+        t_a = dec.decode_step_reference_abi(t_in)
+        t_b = orc2.decode_step(t_in)
+        agree += int(t_a == t_b)
+        t_in = t_b
+    assert agree >= 5, agree
     dec.reset()
     assert dec.position() == 0 and int(dec.k_cache.abs().sum()) == 0
     with pytest.raises(ValueError):

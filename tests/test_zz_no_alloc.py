@@ -5,7 +5,7 @@ plugin inside a host framework that owns all device memory through its own
 arena -- and keeps its hand-off workspace in a static device array of the
 library instead.  This test calls it through the C ABI on two steps in a row
 and checks each step against the allocating entry point
-(launch_a10_int8_decode) fed identical inputs: same argmax token, final RMSNorm
+(launch_a10_int8_decode, via decode_step_reference_abi) fed identical inputs: same argmax token, final RMSNorm
 output and written K/V within the parity tolerance (rel_err <= 1e-2, cosine >=
 0.9998).  The file is named so that pytest collects it last.
 """
@@ -50,7 +50,7 @@ def test_static_workspace_entry_matches_allocating_entry():
             p(dec.lm_head_weight_), p(dec.lm_head_scale_), p(dec.cos_table_), p(dec.sin_table_), p(kc2), p(vc2),
             p(norm2), L, pos, pos + 1, max_seq, ctypes.c_float(dec.attn_scale_), p(dec.d_layer_scales_), stream)
         assert rc == 0, rc
-        ref_tok = dec.decode_step(tok)            # allocating entry point, same inputs
+        ref_tok = dec.decode_step_reference_abi(tok)   # launch_a10_int8_decode, same inputs
         got_tok = int(out2.item())
         assert got_tok == ref_tok, (step, got_tok, ref_tok)
         _close(dec.normalized.cpu(), norm2.cpu())

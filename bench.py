@@ -117,6 +117,49 @@ def build_decoder(L, max_seq, seed=0):
                                        q["model.norm.weight"], cos, sin, L, max_seq)
 
 
+def build_decoder_bf16(L, max_seq, seed=0):
+    import megaqwen_b200 as mq
+    from megaqwen_b200.decoder import layer_lists
+    st = {k: v.to("cuda") for k, v in mq.make_synthetic_state(seed=seed, num_layers=L).items()}
+    layers, _ = layer_lists(st, L, False)
+    cos, sin = mq.make_rope(max_seq, device="cuda")
+    emb = st["model.embed_tokens.weight"]
+    return mq.A10MegakernelDecoder(emb, layers, st["model.norm.weight"], emb, cos, sin, L, max_seq)
+
+
+def run_long_context(args):
+    """one INT8 step at cache length ctx with a KV cache pre-filled
+    with seeded N(0,1) bf16; --steps repetitions of that same step."""
+    ctx, L, K = args.context, args.layers, args.steps
+    dec = build_decoder(L, ctx + 8)
+    g = torch.Generator(device="cuda").manual_seed(ctx)
+    for cache in (dec.k_cache, dec.v_cache):
+        cache[:, :, :ctx].normal_(generator=g)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        dec.set_position(ctx)
+        dec.decode_steps(11, 1)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(K):
+        dec.set_position(ctx)
+        dec.decode_steps(11, 1)
+    b.record(stream)
+    torch.cuda.synchronize()
+    dec.check_device()
+    ms = a.elapsed_time(b) / K
+    alg = BYTES_FIXED + BYTES_PER_POS * (ctx + 1)
+    peak, kind = measured_peak()
+    ach = alg / (ms / 1000.0) / 1e9
+    print(json.dumps({"metric": f"long-context INT8 single-step decode, cache_len {ctx + 1}", "value": round(1000.0 / ms, 2),
+                      "unit": "steps/s", "ms_per_step": round(ms, 4), "steps": K,
+                      "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                   "frac": round(ach / peak, 4), "peak_kind": kind,
+                                   "algorithmic_bytes_per_launch": alg},
+                      "config": {"workload": "config3", "context": ctx, "kv": "seeded N(0,1) bf16"}}), flush=True)
+
+
 def cpu_oracle_rate(L, steps, threads):
     """tok/s of the CPU oracle (reference formulation) over `steps` steps at positions 0..steps-1."""
     import megaqwen_b200 as mq
@@ -164,6 +207,9 @@ def main():
     ap.add_argument("--ncu-case", action="store_true",
                     help="profiling case: 100 untimed steps, then 2 steps (capture with ncu -s 100 -c 1)")
     ap.add_argument("--trace", action="store_true", help="print the per-phase timeline of one step at position 100")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3],
+                    help="BASELINE config: 1 INT8 (default, the headline), 2 BF16 weights, 3 long context")
+    ap.add_argument("--context", type=int, default=4096, help="config 3: cached positions before the timed step")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -184,6 +230,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     torch.cuda.set_device(local)
     from megaqwen_b200 import _lib
+    if args.config == 3:
+        run_long_context(args)
+        return
     if args.ncu_case or args.trace:
         dec = build_decoder(args.layers, 256)
         dec.decode_steps(5, 100)
@@ -198,7 +247,8 @@ def main():
         return
     K, W, L = args.steps, args.warmup, args.layers
     max_seq = max(K, W, 200) + 8
-    dec = build_decoder(L, max_seq)
+    bf16 = args.config == 2
+    dec = build_decoder_bf16(L, max_seq) if bf16 else build_decoder(L, max_seq)
     stream = torch.cuda.current_stream()
     dec.reset()
     dec.decode_steps(4242, W)
@@ -253,24 +303,28 @@ def main():
         positions[str(n)] = round(n / (a.elapsed_time(b) / 1000.0), 1)
     # ---- roofline of the decode kernel (one launch per step) ----
     peak, peak_kind = measured_peak()
-    alg = sum(step_bytes(p) for p in range(K)) / K
+    fixed = 1_192_101_888 if bf16 else BYTES_FIXED
+    alg = sum(fixed + BYTES_PER_POS * (p + 1) for p in range(K)) / K
     achieved = alg / ((ms / 1000.0) / K) / 1e9
-    line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+    metric = METRIC.replace("INT8", "BF16") if bf16 else METRIC
+    line = {"metric": metric, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": round(t_max / K, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8-weights/fp32-accum",
+            "dtype": "bf16-weights/fp32-accum" if bf16 else "int8-weights/fp32-accum",
             "data": "synthetic (seeded N(0,0.02) bf16 weights, 0.1% x20 outliers)",
-            "config": {"workload": f"config1: Qwen3-0.6B batch-1 INT8 greedy decode, {L} layers",
+            "config": {"workload": f"config{args.config}: Qwen3-0.6B batch-1 {'BF16' if bf16 else 'INT8'} greedy decode, {L} layers",
                        "global_batch": world, "seq_len": K, "positions": f"0..{K - 1}",
                        "parallelism": "replicas" if world > 1 else "single",
                        "l2": "inputs larger than L2 (621 MB of weights streamed per step)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic(), "peak_kind": peak_kind,
-                         "kernel": "decode_kernel<W8>", "algorithmic_bytes_per_launch": int(alg)},
+                         "frac": round(achieved / peak, 4), "traffic": None if bf16 else ncu_traffic(),
+                         "peak_kind": peak_kind,
+                         "kernel": "decode_kernel<W16>" if bf16 else "decode_kernel<W8>",
+                         "algorithmic_bytes_per_launch": int(alg)},
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "api": "A10Int8MegakernelDecoder.decode_step(int) -> int"},
+                    "api": ("A10MegakernelDecoder" if bf16 else "A10Int8MegakernelDecoder") + ".decode_step(int) -> int"},
             "tok_s_at_position": positions, "clocks": clk.summary(), "gpu_launches": K,
             "last_token": int(toks[-1].item())}
-    if rank == 0 and not args.no_cpu_baseline and world == 1:
+    if rank == 0 and not args.no_cpu_baseline and world == 1 and not bf16:
         threads = os.cpu_count() or 1
         v = cpu_oracle_rate(L, args.ref_sample_steps, threads)
         line["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "port",

@@ -77,14 +77,14 @@ struct Smem {
     float limb_inv;
     alignas(16) int limb[4][INTER / 4];  // activation limbs of the current matvec phase; row 3 stays zero
     float raw[4 * HD];       // raw q0 q1 k v of this CTA's KV head
-    float q[2][HD];
+    alignas(16) float q[2][HD];
     float m[2], l[2], corr[2];
     float sc[2][32];         // per-warp softmax state during the attention merge
     float pe[2][32];
     float ew[2][32];         // merge weights exp(m_w - M_h)
     float lw_[2][32];        // l_w * ew
     float mx[2];
-    uint16_t kvcur[2][HD];   // current-position K and V, bf16
+    alignas(16) uint16_t kvcur[2][HD];   // current-position K and V, bf16
     unsigned long long best[NCW];
     const void* lw[MAX_LAYERS][11];      // LayerWeights of every layer
     const float* ls[MAX_LAYERS][7];      // ScalePointers of every layer

@@ -720,50 +720,63 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         }
     }
     consumers_sync();
-    // Flash-decode inside the CTA without block barriers: warp w owns the item's
-    // positions past0 + t with t % NCW == w and keeps its own online-softmax
-    // state (m, l, acc) for both GQA heads; lane holds dims 4*lane .. 4*lane+3.
-    float q0[4], q1[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) { q0[j] = sm->q[0][4 * cs.lane + j]; q1[j] = sm->q[1][4 * cs.lane + j]; }
+    // Flash-decode inside the CTA without block barriers.  Warp w owns the item's
+    // ring chunks ci with ci % NCW == w (32 positions each) and keeps its own
+    // online-softmax state (m, l, acc) for both GQA heads.  Within a chunk lane p
+    // scores position p over all 128 dims (dims visited in a lane-rotated order
+    // so the 32 lanes hit different banks), one max/sum reduction per chunk, and
+    // P.V is accumulated with lane holding dims 4*lane .. 4*lane+3.
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     const float scale = P.attn_scale;
-    auto step = [&](const uint16_t* kr, const uint16_t* vr) {
-        const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * cs.lane);
-        const uint2 vw = *reinterpret_cast<const uint2*>(vr + 4 * cs.lane);
-        const float k[4] = {bf16_bits_to_f32(kw.x & 0xffffu), bf16_bits_to_f32(kw.x >> 16),
-                            bf16_bits_to_f32(kw.y & 0xffffu), bf16_bits_to_f32(kw.y >> 16)};
-        const float v[4] = {bf16_bits_to_f32(vw.x & 0xffffu), bf16_bits_to_f32(vw.x >> 16),
-                            bf16_bits_to_f32(vw.y & 0xffffu), bf16_bits_to_f32(vw.y >> 16)};
-        float d0 = q0[0] * k[0] + q0[1] * k[1] + q0[2] * k[2] + q0[3] * k[3];
-        float d1 = q1[0] * k[0] + q1[1] * k[1] + q1[2] * k[2] + q1[3] * k[3];
-        d0 = warp_sum(d0) * scale;
-        d1 = warp_sum(d1) * scale;
-        const float n0 = fmaxf(m0, d0), n1 = fmaxf(m1, d1);
-        const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);
-        const float e0 = expf(d0 - n0), e1 = expf(d1 - n1);
-        l0 = l0 * c0 + e0;
-        l1 = l1 * c1 + e1;
+    const float4* q0v = reinterpret_cast<const float4*>(sm->q[0]);
+    const float4* q1v = reinterpret_cast<const float4*>(sm->q[1]);
+    auto chunk = [&](const uint16_t* kb, const uint16_t* vb, int n) {
+        float s0 = -INFINITY, s1 = -INFINITY;
+        if (cs.lane < n) {
+            const uint16_t* kr = kb + cs.lane * HD;
+            float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+#pragma unroll 8
+            for (int i = 0; i < HD / 4; ++i) {
+                const int d4 = (cs.lane + i) & (HD / 4 - 1);
+                const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * d4);
+                const float k0 = bf16_bits_to_f32(kw.x & 0xffffu), k1 = bf16_bits_to_f32(kw.x >> 16);
+                const float k2 = bf16_bits_to_f32(kw.y & 0xffffu), k3 = bf16_bits_to_f32(kw.y >> 16);
+                const float4 qa = q0v[d4], qb = q1v[d4];
+                x0 = fmaf(qa.x, k0, x0); x1 = fmaf(qa.y, k1, x1); x0 = fmaf(qa.z, k2, x0); x1 = fmaf(qa.w, k3, x1);
+                y0 = fmaf(qb.x, k0, y0); y1 = fmaf(qb.y, k1, y1); y0 = fmaf(qb.z, k2, y0); y1 = fmaf(qb.w, k3, y1);
+            }
+            s0 = (x0 + x1) * scale;
+            s1 = (y0 + y1) * scale;
+        }
+        const float n0 = fmaxf(m0, warp_max(s0)), n1 = fmaxf(m1, warp_max(s1));
+        const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);   // 0 while m is still -inf
+        const float e0 = cs.lane < n ? expf(s0 - n0) : 0.f;
+        const float e1 = cs.lane < n ? expf(s1 - n1) : 0.f;
+        l0 = l0 * c0 + warp_sum(e0);
+        l1 = l1 * c1 + warp_sum(e1);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            a0[j] = fmaf(e0, v[j], a0[j] * c0);
-            a1[j] = fmaf(e1, v[j], a1[j] * c1);
+        for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
+        for (int p = 0; p < n; ++p) {
+            const float ep0 = __shfl_sync(0xffffffffu, e0, p), ep1 = __shfl_sync(0xffffffffu, e1, p);
+            const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * cs.lane);
+            const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
+            const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
+            a0[0] = fmaf(ep0, v0, a0[0]); a0[1] = fmaf(ep0, v1, a0[1]); a0[2] = fmaf(ep0, v2, a0[2]); a0[3] = fmaf(ep0, v3, a0[3]);
+            a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
         }
         m0 = n0;
         m1 = n1;
     };
-    int qi = 0;  // item-relative index of the chunk's first position
-    for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS) {
+    int ci = 0;  // item-relative chunk index
+    for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS, ++ci) {
         const int n = min(KV_CHUNK_POS, G.past1 - p);
         const uint8_t* st = cs.wait(c, 3);
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(st);
-        const uint16_t* vb = reinterpret_cast<const uint16_t*>(st + KV_V_OFFSET);
-        for (int t = ((cs.warp - qi) % NCW + NCW) % NCW; t < n; t += NCW) step(kb + t * HD, vb + t * HD);
+        if (ci % NCW == cs.warp)
+            chunk(reinterpret_cast<const uint16_t*>(st), reinterpret_cast<const uint16_t*>(st + KV_V_OFFSET), n);
         cs.release();
-        qi += n;
     }
-    if (G.owner && qi % NCW == cs.warp) step(sm->kvcur[0], sm->kvcur[1]);  // the current position
+    if (G.owner && ci % NCW == cs.warp) chunk(sm->kvcur[0], sm->kvcur[1], 1);  // the current position
     // Merge the NCW warp states through shared memory (x is free during attention).
     float* wacc = sm->x;  // [NCW][2][HD]
 #pragma unroll

@@ -63,7 +63,8 @@ enum {
     MQ_DEV_OK = 0,
     MQ_DEV_TIMEOUT_EXCHANGE = 1,  /* a tagged-word exchange wait ran out */
     MQ_DEV_TIMEOUT_RING = 2,      /* a weight-ring mbarrier wait ran out */
-    MQ_DEV_BAD_TOKEN = 3          /* on-device token feedback produced an invalid id */
+    MQ_DEV_BAD_TOKEN = 3,         /* an input token id (device-resident) is outside [0, vocab) */
+    MQ_DEV_BAD_POSITION = 4       /* a device-resident position is outside [0, max_seq_len) */
 };
 
 /*
@@ -165,6 +166,54 @@ int mq_decode_multi(
     void* k_cache, void* v_cache, float* g_normalized, float* d_logits, float* d_layer_hidden,
     int num_layers, int position, int max_seq_len, float attn_scale, int row_pad_bytes,
     cudaStream_t stream);
+
+/*
+ * Batched greedy decode (no reference counterpart: the
+ * reference decodes one sequence).  `batch` (<= 64) independent sequences, each
+ * at its own position with its own KV cache, advance num_steps tokens, sharing
+ * one pass over the INT8 weights per step.  The caller owns all memory: the
+ * library allocates nothing on this path.
+ *   - weights: INT8 projections and LM head in the PADDED row layout (row
+ *     stride = row bytes + 16), scales fp32, norms and embedding bf16;
+ *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128];
+ *   - tokens: device int32 [batch]: read as this step's inputs, overwritten
+ *     with the argmax outputs (so repeated steps feed back on the device);
+ *   - positions: device int32 [batch]: position of each sequence's input token
+ *     (cache_len = position + 1); incremented by one per step;
+ *   - workspace: device buffer of mq_batch_workspace_bytes(batch) bytes,
+ *     16-byte aligned, zero-filled before its first use;
+ *   - logits (optional): fp32 [batch][151936] of the last step;
+ *   - max_seq_len <= 32768.
+ * A device-side failure leaves tokens at -1; mq_batch_status() reads the code.
+ * Activations are rounded to bf16 at the inputs of the tensor-core GEMMs.
+ */
+typedef struct MQBatchArgs {
+    const void* embed_weight;
+    const LayerWeights* layer_weights;   /* device array [num_layers] */
+    const ScalePointers* scales;         /* device array [num_layers] */
+    const void* final_norm_weight;
+    const void* lm_head_weight;
+    const float* lm_head_scale;
+    const void* cos_table;
+    const void* sin_table;
+    void* k_cache;
+    void* v_cache;
+    int* tokens;
+    int* positions;
+    void* workspace;
+    size_t workspace_bytes;
+    float* logits;
+    unsigned long long wait_budget_ns;   /* 0: default (2 s) */
+    int batch;
+    int num_layers;
+    int max_seq_len;
+    float attn_scale;
+} MQBatchArgs;
+
+int mq_batch_workspace_bytes(int batch, size_t* bytes);
+int mq_batch_decode(const MQBatchArgs* args, int num_steps, cudaStream_t stream);
+/* Device-side status of a batched workspace (synchronous copy): MQ_DEV_* code. */
+int mq_batch_status(const void* workspace, int* code, int* info);
 
 /*
  * Per-output-channel symmetric INT8 quantizer.  Same arithmetic as

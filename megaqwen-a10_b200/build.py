@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libmqb200.so")
-SOURCES = ["decode_kernel.cu", "quantize.cu"]
+SOURCES = ["decode_kernel.cu", "batch_kernel.cu", "quantize.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

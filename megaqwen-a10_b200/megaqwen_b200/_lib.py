@@ -18,12 +18,14 @@ MQ_ERRORS = {
     -5: "size larger than the entry point supports",
 }
 ROW_PAD = 16  # padding bytes after every weight row in the layout the decoder classes use
-MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 3: "invalid fed-back token"}
+MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 3: "invalid token",
+                 4: "invalid position"}
 
 EXPORTED = (
     "launch_a10_int8_decode", "launch_a10_decode", "mq_decode_multi", "mq_quantize_per_channel",
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
-    "mq_set_trace", "launch_a10_int8_decode_static",
+    "mq_set_trace", "launch_a10_int8_decode_static", "mq_batch_workspace_bytes", "mq_batch_decode",
+    "mq_batch_status",
 )
 
 
@@ -67,6 +69,9 @@ def load():
     lib.mq_set_wait_budget_ns.argtypes = [_u64]
     lib.mq_inject_skip_publish.argtypes = [_i, _i]
     lib.mq_set_trace.argtypes = [_vp, _i]
+    lib.mq_batch_workspace_bytes.argtypes = [_i, ctypes.POINTER(ctypes.c_size_t)]
+    lib.mq_batch_decode.argtypes = [_vp, _i, _vp]
+    lib.mq_batch_status.argtypes = [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]
     lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]
     lib.mq_kernel_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
     for name in EXPORTED:

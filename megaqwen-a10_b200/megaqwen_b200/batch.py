@@ -1,0 +1,95 @@
+"""Batched greedy decode: up to 64 independent sequences,
+each at its own position with its own KV cache, advance one token per step
+while sharing one pass over the INT8 weights (csrc/batch_kernel.cu).
+
+`BatchedDecoder` borrows the padded INT8 weight tables of an
+`A10Int8MegakernelDecoder` and owns the per-sequence state: KV caches
+[B][L][8][max_seq][128] bf16, the token and position vectors and the kernel's
+workspace -- all allocated here with torch, so the C entry point itself
+allocates nothing.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+from .config import HEAD_DIM, NUM_KV_HEADS, VOCAB_SIZE
+
+
+class MQBatchArgs(ctypes.Structure):
+    """Mirror of MQBatchArgs in include/megaqwen_b200.h."""
+    _fields_ = [
+        ("embed_weight", ctypes.c_void_p), ("layer_weights", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+        ("final_norm_weight", ctypes.c_void_p), ("lm_head_weight", ctypes.c_void_p),
+        ("lm_head_scale", ctypes.c_void_p), ("cos_table", ctypes.c_void_p), ("sin_table", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p), ("tokens", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("logits", ctypes.c_void_p), ("wait_budget_ns", ctypes.c_ulonglong), ("batch", ctypes.c_int),
+        ("num_layers", ctypes.c_int), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
+    ]
+
+
+class BatchedDecoder:
+    MAX_BATCH = 64
+
+    def __init__(self, weights, batch, max_seq_len):
+        """weights: an A10Int8MegakernelDecoder (its padded tables are used);
+        max_seq_len <= 32768 and <= the rows of its RoPE tables."""
+        if not 1 <= batch <= self.MAX_BATCH:
+            raise ValueError(f"batch must be in [1, {self.MAX_BATCH}]")
+        if not 1 <= max_seq_len <= min(32768, weights.cos_table_.shape[0]):
+            raise ValueError("max_seq_len out of range")
+        self.w = weights
+        self.device = weights.device
+        self.B, self.L, self.max_seq_len = batch, weights.num_layers_, max_seq_len
+        shape = (batch, self.L, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
+        self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        self.tokens = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(_lib.load().mq_batch_workspace_bytes(batch, ctypes.byref(nbytes)), "mq_batch_workspace_bytes")
+        self.workspace = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
+
+    def set_state(self, tokens, positions):
+        """Input token and position (cache_len = position + 1) of every sequence."""
+        t = torch.as_tensor(tokens, dtype=torch.int32).to(self.device)
+        p = torch.as_tensor(positions, dtype=torch.int32).to(self.device)
+        if t.shape != (self.B,) or p.shape != (self.B,):
+            raise ValueError("tokens and positions must have one entry per sequence")
+        if int(t.min()) < 0 or int(t.max()) >= VOCAB_SIZE:
+            raise ValueError("token out of range")
+        if int(p.min()) < 0 or int(p.max()) >= self.max_seq_len:
+            raise ValueError("position out of range")
+        self.tokens.copy_(t)
+        self.positions.copy_(p)
+
+    def step(self, num_steps=1, logits=None):
+        """Runs num_steps greedy steps for every sequence (on-device token feedback;
+        no host sync).  Returns the device token vector (the last step's outputs)."""
+        if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (self.B, VOCAB_SIZE)):
+            raise ValueError("logits must be fp32 [batch, vocab]")
+        w = self.w
+        a = MQBatchArgs(w.embed_weight_.data_ptr(), w.d_layer_weights_pad_.data_ptr(), w.d_layer_scales_.data_ptr(),
+                        w.final_norm_weight_.data_ptr(), w.lm_head_pad_.data_ptr(), w.lm_head_scale_.data_ptr(),
+                        w.cos_table_.data_ptr(), w.sin_table_.data_ptr(), self.k_cache.data_ptr(),
+                        self.v_cache.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
+                        self.workspace.data_ptr(), self.workspace.numel(),
+                        logits.data_ptr() if logits is not None else None, 0, self.B, self.L,
+                        self.max_seq_len, w.attn_scale_)
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            rc = _lib.load().mq_batch_decode(ctypes.byref(a), int(num_steps), ctypes.c_void_p(stream))
+        _lib.check(rc, "mq_batch_decode")
+        return self.tokens
+
+    def status(self):
+        code, info = ctypes.c_int(0), ctypes.c_int(0)
+        _lib.check(_lib.load().mq_batch_status(ctypes.c_void_p(self.workspace.data_ptr()), ctypes.byref(code),
+                                               ctypes.byref(info)), "mq_batch_status")
+        return code.value, info.value
+
+    def check_device(self):
+        code, info = self.status()
+        if code:
+            raise _lib.MQError(f"batched decode: device error {code} ({_lib.MQ_DEV_ERRORS.get(code, '?')}, at {info})")

@@ -203,6 +203,8 @@ typedef struct MQBatchArgs {
     void* workspace;
     size_t workspace_bytes;
     float* logits;
+    unsigned long long* trace;           /* optional diagnostics: [num_ctas][8*(num_layers+1)] %globaltimer
+                                            stamps, slot layer*8+phase (1 QKV .. 6 down done), 8L+6/7 LM */
     unsigned long long wait_budget_ns;   /* 0: default (2 s) */
     int batch;
     int num_layers;

@@ -64,6 +64,7 @@ struct Params {
     unsigned long long* best;   // [B]
     unsigned int* ctl;          // [0] barrier counter, [1] exit counter, [2] error code, [3] error info
     float* logits;              // optional [B][VOCAB]
+    unsigned long long* trace;  // optional [gridDim.x][8 * (L + 1)] globaltimer stamps
     unsigned long long budget_ns;
     int B, L, max_seq;
     float attn_scale;
@@ -73,7 +74,7 @@ struct Params {
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
 struct GemmSmem {
-    alignas(16) __nv_bfloat16 xs[2][BMAX][XS_STRIDE];                  // hi and lo planes, 133 KB
+    alignas(16) __nv_bfloat16 xs[2 * BMAX * XS_STRIDE];  // hi and lo planes, viewed as [2][ntok][width + 8], 133 KB
     alignas(16) uint8_t w[2][GROUP_ROWS * (HIDDEN + ROW_SKEW)];        // 2 x 33 KB
 };
 struct AttnSmem {
@@ -111,6 +112,11 @@ __device__ __noinline__ void fail(Ctx& c, int code, int info) {
 
 // Bounded grid barrier (release/acquire on a monotone counter reset per launch).
 // Returns false when any CTA has failed; the caller then leaves the step.
+__device__ __forceinline__ void stamp(const Ctx& c, int slot) {
+    if (c.P->trace && threadIdx.x == 0)
+        c.P->trace[(size_t)blockIdx.x * 8 * (c.P->L + 1) + slot] = globaltimer();
+}
+
 __device__ bool grid_barrier(Ctx& c, int where) {
     // Shared-memory bytes written through the generic proxy in this phase may be
     // overwritten by bulk copies (async proxy) in the next one.
@@ -180,34 +186,108 @@ __device__ __forceinline__ bool mbar_wait_b(Ctx& c, uint64_t* bar, uint32_t pari
     }
 }
 
-// x -> (hi, lo) bf16 planes of the staged slab.
-__device__ __forceinline__ void put_x(Smem* sm, int b, int k, float x) {
-    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
-    sm->g.xs[0][b][k] = hi;
-    sm->g.xs[1][b][k] = __float2bfloat16_rn(x - __bfloat162float(hi));
+// Writes 16 consecutive values (this lane's part of a 512-wide slab row) as hi/lo.
+// Staged activations: xs viewed as [2][ntok][width + 8] (plane 0 = hi, 1 = lo).
+template <int NTOK, int WIDTH>
+struct XView {
+    static constexpr int RS = WIDTH + 8;
+    static constexpr int PS = NTOK * RS;
+    static_assert(2 * PS <= 2 * BMAX * XS_STRIDE, "view exceeds the staging buffer");
+};
+template <int NTOK, int WIDTH>
+__device__ __forceinline__ void put16(Smem* sm, int b, int k0, const float (&v)[16]) {
+    using V = XView<NTOK, WIDTH>;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(v[i], v[i + 1]);
+        const float2 hf = __bfloat1622float2(hi);
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v[i] - hf.x, v[i + 1] - hf.y);
+        *reinterpret_cast<__nv_bfloat162*>(&sm->g.xs[b * V::RS + k0 + i]) = hi;
+        *reinterpret_cast<__nv_bfloat162*>(&sm->g.xs[V::PS + b * V::RS + k0 + i]) = lo;
+    }
 }
 
-// Stages slab s (columns [s*SLAB, (s+1)*SLAB)) of X = RMSNorm(src[b]) * w for the
-// B sequences (rows >= B are zero).  src(b, k) gives the fp32 input; the
-// per-sequence rstd is computed at s == 0 and kept in shared memory.
-template <class Src>
-__device__ __forceinline__ void stage_norm_slab(Smem* sm, int B, int s, const __nv_bfloat16* w, Src src) {
+// Loads 16 fp32 values [k0, k0 + 16) of a row (4 x float4, all issued together).
+__device__ __forceinline__ void load16(const float* row, int k0, float (&v)[16]) {
+    const float4* r = reinterpret_cast<const float4*>(row + k0);
+    float4 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = __ldcg(r + i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { v[4 * i] = q[i].x; v[4 * i + 1] = q[i].y; v[4 * i + 2] = q[i].z; v[4 * i + 3] = q[i].w; }
+}
+__device__ __forceinline__ void load16_bf16(const __nv_bfloat16* row, int k0, float (&v)[16]) {
+    const uint4* r = reinterpret_cast<const uint4*>(row + k0);
+    const uint4 a = __ldg(r), b = __ldg(r + 1);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { v[2 * i] = bf16_bits_to_f32(w[i] & 0xffffu); v[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16); }
+}
+
+// Stages slab s (columns [s*SLAB, (s+1)*SLAB)) of X = RMSNorm(row_b) * w for the
+// B sequences (rows >= B are zero); row(b) is the fp32 row of sequence b, or the
+// bf16 embedding row when emb is set.  rstd is computed at s == 0 and kept in
+// shared memory.  Lane l owns columns [16l, 16l + 16) of the slab.
+template <bool EMB, class Row>
+__device__ __forceinline__ void stage_norm_slab(Smem* sm, int B, int s, const __nv_bfloat16* w, Row row) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (s == 0) {
         for (int b = warp; b < B; b += NW) {
+            float v0[16], v1[16];
+            if constexpr (EMB) { load16_bf16(row(b), 16 * lane, v0); load16_bf16(row(b), 512 + 16 * lane, v1); }
+            else { load16(row(b), 16 * lane, v0); load16(row(b), 512 + 16 * lane, v1); }
             float ss = 0.f;
-            for (int k = lane; k < HIDDEN; k += 32) { const float v = src(b, k); ss += v * v; }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss += v0[i] * v0[i] + v1[i] * v1[i];
             ss = warp_sum(ss);
             if (lane == 0) sm->rstd[b] = rsqrtf(ss / (float)HIDDEN + RMS_EPS);
         }
         __syncthreads();
     }
+    float wv[16];
+    load16_bf16(w, s * SLAB + 16 * lane, wv);
     for (int b = warp; b < BMAX; b += NW) {
-        const float r = b < B ? sm->rstd[b] : 0.f;
-        for (int kk = lane; kk < SLAB; kk += 32) {
-            const int k = s * SLAB + kk;
-            put_x(sm, b, kk, b < B ? src(b, k) * r * __bfloat162float(w[k]) : 0.f);
+        float v[16];
+        if (b < B) {
+            if constexpr (EMB) load16_bf16(row(b), s * SLAB + 16 * lane, v);
+            else load16(row(b), s * SLAB + 16 * lane, v);
+            const float r = sm->rstd[b];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = v[i] * r * wv[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
         }
+        put16<BMAX, SLAB>(sm, b, 16 * lane, v);
+    }
+}
+
+// LM head: X = RMSNorm(h[n0 + i]) * w for 32 tokens, full width (lane owns
+// columns [32 lane, 32 lane + 32)).
+__device__ __forceinline__ void stage_norm_half(Smem* sm, int B, int n0, const float* h, const __nv_bfloat16* w) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float w0[16], w1[16];
+    load16_bf16(w, 32 * lane, w0);
+    load16_bf16(w, 32 * lane + 16, w1);
+    for (int i = warp; i < 32; i += NW) {
+        const int b = n0 + i;
+        float v0[16], v1[16];
+        if (b < B) {
+            load16(h + (size_t)b * HIDDEN, 32 * lane, v0);
+            load16(h + (size_t)b * HIDDEN, 32 * lane + 16, v1);
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) ss += v0[k] * v0[k] + v1[k] * v1[k];
+            ss = warp_sum(ss);
+            const float r = rsqrtf(ss / (float)HIDDEN + RMS_EPS);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) { v0[k] *= r * w0[k]; v1[k] *= r * w1[k]; }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v0[k] = v1[k] = 0.f;
+        }
+        put16<32, HIDDEN>(sm, i, 32 * lane, v0);
+        put16<32, HIDDEN>(sm, i, 32 * lane + 16, v1);
     }
 }
 
@@ -215,12 +295,13 @@ __device__ __forceinline__ void stage_norm_slab(Smem* sm, int B, int s, const __
 __device__ __forceinline__ void stage_copy(Smem* sm, int B, const float* src, int K, int s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int b = warp; b < BMAX; b += NW) {
-        const float4* r = reinterpret_cast<const float4*>(src + (size_t)b * K + (size_t)s * SLAB);
-        for (int j = lane; j < SLAB / 4; j += 32) {
-            const float4 v = b < B ? __ldcg(r + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-            put_x(sm, b, 4 * j + 0, v.x); put_x(sm, b, 4 * j + 1, v.y);
-            put_x(sm, b, 4 * j + 2, v.z); put_x(sm, b, 4 * j + 3, v.w);
+        float v[16];
+        if (b < B) load16(src + (size_t)b * K, s * SLAB + 16 * lane, v);
+        else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
         }
+        put16<BMAX, SLAB>(sm, b, 16 * lane, v);
     }
 }
 
@@ -235,20 +316,25 @@ __device__ __forceinline__ void load_rows(Smem* sm, int buf, const uint8_t* src,
 // stage(s).  SETS = 1: plain rows (tile i = smem rows 16i..16i+15); SETS = 2:
 // gate/up (tile i: gate rows at smem 32i.., up rows at 32i+16..), two
 // accumulators per unit.  epi(row_in_group, token, value[SETS]).
-template <int K, int SETS, class Stage, class Epi>
+template <int K, int SETS, int NTOK = BMAX, int WIDTH = SLAB, class Stage, class Epi>
 __device__ bool gemm_group(Ctx& c, int buf, uint32_t& wuse, int rows, Stage stage, Epi epi) {
-    constexpr int NS = K / SLAB;
+    constexpr int NS = K / WIDTH;
     constexpr int RS = K + ROW_SKEW;
+    constexpr int NJ = NTOK / 8;      // n-tiles
+    using V = XView<NTOK, WIDTH>;
     Smem* sm = c.sm;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int T = (rows + 15) / 16;
-    const int nunits = T * 8;   // <= 16 for every group here
-    float acc[2][SETS][4];
+    const int nunits = T * NJ;   // <= 16 for every group here
+    // four independent accumulation chains per unit and set: (hi, lo) x (even, odd k-step)
+    float acc[2][SETS][4][4];
 #pragma unroll
     for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int q = 0; q < SETS; ++q) acc[k][q][0] = acc[k][q][1] = acc[k][q][2] = acc[k][q][3] = 0.f;
+        for (int q = 0; q < SETS; ++q)
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) acc[k][q][ch][0] = acc[k][q][ch][1] = acc[k][q][ch][2] = acc[k][q][ch][3] = 0.f;
     bool ok = true;
     for (int s = 0; s < NS; ++s) {
         if (s > 0) __syncthreads();
@@ -263,23 +349,25 @@ __device__ bool gemm_group(Ctx& c, int buf, uint32_t& wuse, int rows, Stage stag
         for (int k = 0; k < 2; ++k) {
             const int u = warp + k * NW;
             if (u >= nunits) continue;
-            const int tile = u >> 3, j = u & 7;
-            const __nv_bfloat16* xh = sm->g.xs[0][j * 8 + g];
-            const __nv_bfloat16* xl = sm->g.xs[1][j * 8 + g];
+            const int tile = u / NJ, j = u % NJ;
+            const __nv_bfloat16* xh = sm->g.xs + (j * 8 + g) * V::RS;
+            const __nv_bfloat16* xl = xh + V::PS;
 #pragma unroll
             for (int q = 0; q < SETS; ++q) {
                 const int base = SETS == 1 ? tile * 16 : tile * 32 + q * 16;
                 const int lim = SETS == 1 ? rows - 1 : base + 15;
-                const uint8_t* ra = w + (size_t)min(base + g, lim) * RS + (size_t)s * SLAB;
-                const uint8_t* rb = w + (size_t)min(base + g + 8, lim) * RS + (size_t)s * SLAB;
-#pragma unroll 4
-                for (int ks = 0; ks < SLAB / 16; ++ks) {
-                    uint32_t a[4];
-                    load_a(a, ra, rb, ks * 16, t);
-                    mma_bf16(acc[k][q], a, *reinterpret_cast<const uint32_t*>(xh + ks * 16 + 2 * t),
-                             *reinterpret_cast<const uint32_t*>(xh + ks * 16 + 8 + 2 * t));
-                    mma_bf16(acc[k][q], a, *reinterpret_cast<const uint32_t*>(xl + ks * 16 + 2 * t),
-                             *reinterpret_cast<const uint32_t*>(xl + ks * 16 + 8 + 2 * t));
+                const uint8_t* ra = w + (size_t)min(base + g, lim) * RS + (size_t)s * WIDTH;
+                const uint8_t* rb = w + (size_t)min(base + g + 8, lim) * RS + (size_t)s * WIDTH;
+#pragma unroll 2
+                for (int ks = 0; ks < WIDTH / 16; ks += 2) {
+                    uint32_t a0[4], a1[4];
+                    load_a(a0, ra, rb, ks * 16, t);
+                    load_a(a1, ra, rb, ks * 16 + 16, t);
+                    const int k0 = ks * 16 + 2 * t;
+                    mma_bf16(acc[k][q][0], a0, *reinterpret_cast<const uint32_t*>(xh + k0), *reinterpret_cast<const uint32_t*>(xh + k0 + 8));
+                    mma_bf16(acc[k][q][1], a0, *reinterpret_cast<const uint32_t*>(xl + k0), *reinterpret_cast<const uint32_t*>(xl + k0 + 8));
+                    mma_bf16(acc[k][q][2], a1, *reinterpret_cast<const uint32_t*>(xh + k0 + 16), *reinterpret_cast<const uint32_t*>(xh + k0 + 24));
+                    mma_bf16(acc[k][q][3], a1, *reinterpret_cast<const uint32_t*>(xl + k0 + 16), *reinterpret_cast<const uint32_t*>(xl + k0 + 24));
                 }
             }
         }
@@ -288,14 +376,15 @@ __device__ bool gemm_group(Ctx& c, int buf, uint32_t& wuse, int rows, Stage stag
     for (int k = 0; k < 2; ++k) {
         const int u = warp + k * NW;
         if (u >= nunits) continue;
-        const int tile = u >> 3, j = u & 7;
+        const int tile = u / NJ, j = u % NJ;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int r = tile * 16 + g + (e >= 2 ? 8 : 0);
             const int n = j * 8 + 2 * t + (e & 1);
             float v[SETS];
 #pragma unroll
-            for (int q = 0; q < SETS; ++q) v[q] = acc[k][q][e];
+            for (int q = 0; q < SETS; ++q)
+                v[q] = (acc[k][q][0][e] + acc[k][q][1][e]) + (acc[k][q][2][e] + acc[k][q][3][e]);
             if (r < rows) epi(r, n, v);
         }
     }
@@ -519,12 +608,13 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                 const __nv_bfloat16* nw = (const __nv_bfloat16*)w.input_layernorm_weight;
                 if (l == 0) {
                     // h = embedding rows; CTA 0 also stores them as the fp32 residual.
-                    auto src = [&](int b, int k) { return __bfloat162float(P.embed[(size_t)P.tokens_in[b] * HIDDEN + k]); };
-                    stage_norm_slab(sm, B, s_, nw, src);
+                    auto row = [&](int b) { return P.embed + (size_t)P.tokens_in[b] * HIDDEN; };
+                    stage_norm_slab<true>(sm, B, s_, nw, row);
                     if (cta == 0 && s_ == 0)
-                        for (int i = threadIdx.x; i < B * HIDDEN; i += NT) P.h[i] = src(i / HIDDEN, i % HIDDEN);
+                        for (int i = threadIdx.x; i < B * HIDDEN; i += NT)
+                            P.h[i] = __bfloat162float(P.embed[(size_t)P.tokens_in[i / HIDDEN] * HIDDEN + i % HIDDEN]);
                 } else {
-                    stage_norm_slab(sm, B, s_, nw, [&](int b, int k) { return __ldcg(P.h + (size_t)b * HIDDEN + k); });
+                    stage_norm_slab<false>(sm, B, s_, nw, [&](int b) { return (const float*)P.h + (size_t)b * HIDDEN; });
                 }
             };
             const float* sq = sc.q_scale; const float* sk = sc.k_scale; const float* sv = sc.v_scale;
@@ -535,6 +625,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                 P.qkv[(size_t)n * QKV_ROWS + row] = v[0] * s_;
             }) && ok;
         }
+        stamp(c, l * 8 + 1);
         if (!grid_barrier(c, 1)) { ok = false; break; }
         // ---- attention ----
         {
@@ -553,9 +644,11 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                 ++b;
             }
         }
+        stamp(c, l * 8 + 2);
         if (!grid_barrier(c, 2)) { ok = false; break; }
         // ---- merge ----
         for (int it = cta * NW + warp; it < B * NQH; it += nb * NW) merge_item(P, it / NQH, it % NQH);
+        stamp(c, l * 8 + 3);
         if (!grid_barrier(c, 3)) { ok = false; break; }
         // ---- O + residual ----
         {
@@ -574,6 +667,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                       P.act[i] = v[0] * so[r0 + r] + __ldcg(P.h + i);
                                   }) && ok;
         }
+        stamp(c, l * 8 + 4);
         if (!grid_barrier(c, 4)) { ok = false; break; }
         // ---- gate/up + SiLU ----
         {
@@ -591,8 +685,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                 }
                 ok = gemm_group<HIDDEN, 2>(c, buf, wuse[buf], np,
                                            [&](int s_) {
-                                               stage_norm_slab(sm, B, s_, (const __nv_bfloat16*)w.post_attn_layernorm_weight,
-                                                               [&](int b, int k) { return __ldcg(P.act + (size_t)b * HIDDEN + k); });
+                                               stage_norm_slab<false>(sm, B, s_, (const __nv_bfloat16*)w.post_attn_layernorm_weight,
+                                                                      [&](int b) { return (const float*)P.act + (size_t)b * HIDDEN; });
                                            },
                                            [&](int r, int n, const float* v) {
                                                if (n >= B) return;
@@ -603,6 +697,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                            }) && ok;
             }
         }
+        stamp(c, l * 8 + 5);
         if (!grid_barrier(c, 5)) { ok = false; break; }
         // ---- down + residual -> h ----
         {
@@ -621,9 +716,12 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                       P.h[i] = __bfloat162float(__float2bfloat16_rn(v[0] * sd[r0 + r] + __ldcg(P.act + i)));
                                   }) && ok;
         }
+        stamp(c, l * 8 + 6);
         if (!grid_barrier(c, 6)) { ok = false; break; }
     }
     // ---- final norm + LM head + per-sequence argmax ----
+    // Two halves of 32 sequences: each half's normalised activations are staged
+    // once at full width and all of this CTA's LM-head rows stream past them.
     if (ok) {
         constexpr int RS = HIDDEN + ROW_SKEW;
         const int r0 = split_lo(VOCAB, nb, cta), r1 = split_lo(VOCAB, nb, cta + 1);
@@ -633,31 +731,38 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             mbar_arrive_expect_tx(&sm->wbar[buf], (uint32_t)(n * RS));
             copy_rows(sm, buf, P.lm_w, gr0, n, RS, 0);
         };
-        if (threadIdx.x == 0) issue(r0, 0);
-        for (int gr = r0, gi = 0; gr < r1 && ok; gr += GROUP_ROWS, ++gi) {
-            const int buf = gi & 1;
-            const int n = min(GROUP_ROWS, r1 - gr);
-            // the other buffer was released by the previous group's trailing barrier
-            if (threadIdx.x == 0 && gr + GROUP_ROWS < r1) issue(gr + GROUP_ROWS, buf ^ 1);
-            ok = gemm_group<HIDDEN, 1>(c, buf, wuse[buf], n,
-                                       [&](int s_) {
-                                           stage_norm_slab(sm, B, s_, P.final_norm,
-                                                           [&](int b, int k) { return __ldcg(P.h + (size_t)b * HIDDEN + k); });
-                                       },
-                                       [&](int r, int tok, const float* v) {
-                                           if (tok >= B) return;
-                                           const int row = gr + r;
-                                           const float lg = v[0] * P.lm_scale[row];
-                                           if (P.logits) P.logits[(size_t)tok * VOCAB + row] = lg;
-                                           const unsigned long long key =
-                                               (((unsigned long long)float_order_key(lg)) << 32) | (uint32_t)(~(uint32_t)row);
-                                           atomicMax(&sm->tokbest[tok], key);
-                                       }) && ok;
+        const int halves = (B + 31) / 32;
+        int gi = 0;
+        for (int hf = 0; hf < halves && ok; ++hf) {
+            const int n0 = hf * 32;
+            if (threadIdx.x == 0) issue(r0, gi & 1);
+            for (int gr = r0; gr < r1 && ok; gr += GROUP_ROWS, ++gi) {
+                const int buf = gi & 1;
+                const int n = min(GROUP_ROWS, r1 - gr);
+                // the other buffer was released by the previous group's trailing barrier
+                if (threadIdx.x == 0 && gr + GROUP_ROWS < r1) issue(gr + GROUP_ROWS, buf ^ 1);
+                const bool first = gr == r0;
+                ok = gemm_group<HIDDEN, 1, 32, HIDDEN>(
+                         c, buf, wuse[buf], n,
+                         [&](int) { if (first) stage_norm_half(sm, B, n0, P.h, P.final_norm); },
+                         [&](int r, int tl, const float* v) {
+                             const int tok = n0 + tl;
+                             if (tok >= B) return;
+                             const int row = gr + r;
+                             const float lg = v[0] * P.lm_scale[row];
+                             if (P.logits) P.logits[(size_t)tok * VOCAB + row] = lg;
+                             const unsigned long long key =
+                                 (((unsigned long long)float_order_key(lg)) << 32) | (uint32_t)(~(uint32_t)row);
+                             atomicMax(&sm->tokbest[tok], key);
+                         }) && ok;
+            }
         }
         __syncthreads();
         for (int t = threadIdx.x; t < B; t += NT) atomicMax(&P.best[t], sm->tokbest[t]);
     }
+    stamp(c, P.L * 8 + 6);
     grid_barrier(c, 7);
+    stamp(c, P.L * 8 + 7);
     if (cta == 0) {
         const bool err = ld_relaxed32(&P.ctl[2]) != 0;
         for (int t = threadIdx.x; t < B; t += NT) {
@@ -767,6 +872,7 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     P.best = (unsigned long long*)(ws + Lw.best);
     P.ctl = (unsigned*)(ws + Lw.ctl);
     P.logits = a->logits;
+    P.trace = a->trace;
     P.budget_ns = a->wait_budget_ns ? a->wait_budget_ns : 2000000000ull;
     P.B = a->batch;
     P.L = a->num_layers;

@@ -24,7 +24,8 @@ class MQBatchArgs(ctypes.Structure):
         ("lm_head_scale", ctypes.c_void_p), ("cos_table", ctypes.c_void_p), ("sin_table", ctypes.c_void_p),
         ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p), ("tokens", ctypes.c_void_p),
         ("positions", ctypes.c_void_p), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
-        ("logits", ctypes.c_void_p), ("wait_budget_ns", ctypes.c_ulonglong), ("batch", ctypes.c_int),
+        ("logits", ctypes.c_void_p), ("trace", ctypes.c_void_p), ("wait_budget_ns", ctypes.c_ulonglong),
+        ("batch", ctypes.c_int),
         ("num_layers", ctypes.c_int), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
     ]
 
@@ -64,7 +65,7 @@ class BatchedDecoder:
         self.tokens.copy_(t)
         self.positions.copy_(p)
 
-    def step(self, num_steps=1, logits=None):
+    def step(self, num_steps=1, logits=None, trace=None):
         """Runs num_steps greedy steps for every sequence (on-device token feedback;
         no host sync).  Returns the device token vector (the last step's outputs)."""
         if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (self.B, VOCAB_SIZE)):
@@ -75,7 +76,8 @@ class BatchedDecoder:
                         w.cos_table_.data_ptr(), w.sin_table_.data_ptr(), self.k_cache.data_ptr(),
                         self.v_cache.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
                         self.workspace.data_ptr(), self.workspace.numel(),
-                        logits.data_ptr() if logits is not None else None, 0, self.B, self.L,
+                        logits.data_ptr() if logits is not None else None,
+                        trace.data_ptr() if trace is not None else None, 0, self.B, self.L,
                         self.max_seq_len, w.attn_scale_)
         with torch.cuda.device(self.device):
             stream = torch.cuda.current_stream(self.device).cuda_stream

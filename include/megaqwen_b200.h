@@ -173,8 +173,9 @@ int mq_decode_multi(
  * at its own position with its own KV cache, advance num_steps tokens, sharing
  * one pass over the INT8 weights per step.  The caller owns all memory: the
  * library allocates nothing on this path.
- *   - weights: INT8 projections and LM head in the PADDED row layout (row
- *     stride = row bytes + 16), scales fp32, norms and embedding bf16;
+ *   - weights: INT8 projections and LM head TILE-PACKED by
+ *     mq_pack_weight_tiles (LayerWeights / lm_head_weight point at the packed
+ *     copies), scales fp32, norms and embedding bf16;
  *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128];
  *   - tokens: device int32 [batch]: read as this step's inputs, overwritten
  *     with the argmax outputs (so repeated steps feed back on the device);
@@ -185,7 +186,9 @@ int mq_decode_multi(
  *   - logits (optional): fp32 [batch][151936] of the last step;
  *   - max_seq_len <= 32768.
  * A device-side failure leaves tokens at -1; mq_batch_status() reads the code.
- * Activations are rounded to bf16 at the inputs of the tensor-core GEMMs.
+ * The GEMMs run on the tcgen05 tensor cores with bf16 operands: INT8 weights
+ * are dequantised exactly to bf16 in shared memory; each activation enters as
+ * two bf16 parts, hi + lo (about 16 significant bits); fp32 accumulation.
  */
 typedef struct MQBatchArgs {
     const void* embed_weight;
@@ -216,6 +219,28 @@ int mq_batch_workspace_bytes(int batch, size_t* bytes);
 int mq_batch_decode(const MQBatchArgs* args, int num_steps, cudaStream_t stream);
 /* Device-side status of a batched workspace (synchronous copy): MQ_DEV_* code. */
 int mq_batch_status(const void* workspace, int* code, int* info);
+
+/*
+ * Packs an INT8 weight matrix [rows][K] (row stride src_row_stride bytes,
+ * a multiple of 8) for the batched path: 16-row x 64-column blocks of 1 KB,
+ * block (tile, kb) at byte ((tile * K/64) + kb) * 1024, inside ordered
+ * [8-column group][16 rows][8 bytes].  rows % 16 == 0, K % 64 == 0; dst holds
+ * rows * K bytes, 16-byte aligned.  Asynchronous on `stream`.
+ */
+int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
+                         cudaStream_t stream);
+
+/*
+ * The batched path's tensor-core GEMM on its own:
+ * y[t][m] = scale[m] * sum_k W[m][k] * x[t][k] for t < B <= 64, W tile-packed
+ * [M][K] INT8 (M % 16 == 0, K in {1024, 2048, 3072}), x fp32 [B][K], y fp32
+ * [B][M]; workspace of mq_batch_matmul_workspace_bytes(K) bytes, 16-byte
+ * aligned.  Asynchronous on `stream`; mq_batch_status(workspace) reads a
+ * device-side timeout.
+ */
+int mq_batch_matmul_workspace_bytes(int K, size_t* bytes);
+int mq_batch_matmul(const int8_t* w_tiles, const float* scale, const float* x, float* y, int M, int K, int B,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Per-output-channel symmetric INT8 quantizer.  Same arithmetic as

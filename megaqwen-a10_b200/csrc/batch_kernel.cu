@@ -1,45 +1,75 @@
 // batch_kernel.cu -- batched greedy decode of Qwen3-0.6B on B200 (sm_100a):
-// B independent sequences (each at its own position, with its own KV cache)
-// advance one token per launch, sharing one pass over the INT8 weights.
+// B <= 64 independent sequences (each at its own position, with its own KV
+// cache) advance one token per launch, sharing one pass over the INT8 weights.
 //
 // Per layer six phases separated by bounded grid barriers (a batched step is
-// KV-bound, ~1 ms, so ~1.2 us per barrier is affordable and all data can move
-// through plain global buffers):
-//   QKV   X = bf16(RMSNorm(h)) staged in shared memory; weight-stationary GEMM
-//         on the tensor cores (mma.sync m16n8k16 bf16): INT8 weight rows are
-//         dequantised to bf16 exactly in registers, the per-row scale is
-//         applied in the epilogue  -> qkv[b][4096] fp32
+// KV-bound, milliseconds, so ~1.2 us per barrier is affordable and all data
+// moves through plain global buffers):
+//   QKV   GEMM on the 5th-generation tensor cores (tcgen05.mma, accumulator in
+//         TMEM) -> qkv[b][4096] fp32
 //   ATTN  one warp per (sequence, KV head, 256-position split): QK-RMSNorm +
 //         RoPE at the sequence's own position, K/V write, flash-decode over
 //         the cached positions (KV chunks bulk-copied into the warp's shared
 //         buffer)  -> split partials (m, l, acc)
-//   MERGE one warp per (sequence, q head): merges the splits -> attn bf16
-//   O     GEMM + residual -> act fp32
-//   GU    X = bf16(RMSNorm(act)); gate and up GEMM, SiLU(gate)*up -> mlp bf16
+//   MERGE one warp per (sequence, q head): merges the splits -> O operand
+//   O     GEMM + residual -> act fp32, GU operand
+//   GU    gate and up GEMM, SiLU(gate)*up -> DOWN operand
 //   DOWN  GEMM + residual -> h (rounded to bf16, as between layers of the
-//         batch-1 kernel)
-// then RMSNorm + LM-head GEMM with a per-sequence packed argmax.
-// Activations enter the tensor cores as two bf16 parts, x = hi + lo (about 16
-// significant bits), each multiplied by the exactly dequantised bf16 weights
-// with fp32 accumulation.
+//         batch-1 kernel), next QKV (or LM-head) operand
+// then the LM-head GEMM with a per-sequence packed argmax.
+//
+// GEMM shape.  D[128 x N] = X[128 x K] * W[N x K]^T with M = 128 rows of
+// activations: rows 0..63 hold the bf16 "hi" parts of the 64 sequences, rows
+// 64..127 the bf16 "lo" parts (x = hi + lo carries ~16 significant bits), so
+// one MMA covers both and the epilogue adds row t and row 64 + t.  N = this
+// CTA's weight rows (16-row tiles, N <= 256), K streamed in slabs through a
+// three-slot shared-memory ring fed by bulk copies:
+//   * the activation operand lives in global memory already in the tensor
+//     core's K-major no-swizzle layout (8-wide k columns of [128 rows][16 B]),
+//     written by the producing phase's epilogue, so a slab is ONE bulk copy;
+//   * the INT8 weights are tile-packed once at load time (16 rows x 64 k per
+//     1 KB block, in [8-k column][row][8 B] order), so a slab of a tile is one
+//     bulk copy; the CTA dequantises it to bf16 (exact) in shared memory in the
+//     same K-major layout and one thread issues the tcgen05.mma instructions;
+//   * the per-row weight scale (and, for RMSNorm inputs, the per-sequence
+//     1/rms) multiply the fp32 accumulator in the epilogue, read back from
+//     TMEM with tcgen05.ld.
+// RMSNorm inputs are written as h*w (norm weight applied, 1/rms not) together
+// with per-16-row partial sums of squares; the consumer reduces the 64 partials
+// in a fixed order, so results are deterministic.
 #include "common.cuh"
 #include <stdlib.h>
 
 namespace mq {
 namespace batch {
 
-constexpr int BMAX = 64;                 // sequences per launch (8 mma n-tiles)
+constexpr int BMAX = 64;                 // sequences per launch
 constexpr int NW = 12;                   // warps per CTA
 constexpr int NT = NW * 32;
-constexpr int SLAB = 512;                // k columns staged at a time
-constexpr int XS_STRIDE = SLAB + 8;      // bf16 elements per staged activation row (16-byte skew)
+constexpr int MROWS = 128;               // MMA M: 64 hi rows + 64 lo rows
+constexpr int XCOL = MROWS * 16;         // bytes of one 8-wide k column of the activation operand
+constexpr int TROWS = 16;                // weight rows per packed tile
+constexpr int KBLK = 64;                 // k per packed 1 KB block
+constexpr int NR = 3;                    // ring slots
+constexpr int SLOT = 64 * 1024;          // bytes per ring slot
+constexpr int TMEM_COLS = 256;           // fp32 accumulator columns (N <= 256)
+constexpr int MAX_TILES_PASS = TMEM_COLS / TROWS;
+constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension (sum-of-squares partials)
 constexpr int SPLIT_POS = 256;           // attention positions per warp item
 constexpr int MAX_SPLITS_B = 128;        // per sequence: max_seq <= 32768
 constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
-constexpr int GROUP_ROWS = 32;           // weight rows staged per GEMM group (K = 1024)
+
+// Ring slot contents for slab width KS and N weight rows: activation slab
+// (128 x KS bf16), dequantised weight slab (N x KS bf16), raw weight slab (N x KS int8).
+template <int KS>
+struct SlabGeom {
+    static constexpr int A_BYTES = MROWS * KS * 2;
+    static constexpr int MAX_N = (SLOT - A_BYTES) / (3 * KS);
+};
+static_assert(SlabGeom<128>::MAX_N >= 64 && SlabGeom<64>::MAX_N >= 256, "ring slot too small");
 
 struct Params {
-    // weights (padded rows: stride = row bytes + ROW_SKEW)
+    // weights: INT8 matrices tile-packed (mq_pack_weight_tiles)
     const __nv_bfloat16* embed;
     const LayerWeights* layers;
     const ScalePointers* scales;
@@ -55,11 +85,15 @@ struct Params {
     int* tokens_out;            // [B]
     int* positions;             // [B] position of the token being decoded (cache_len = pos + 1); advanced by 1 per step
     // workspace
-    float* h;                   // [B][1024]
-    float* act;                 // [B][1024]
+    float* h;                   // [B][1024] residual stream
+    float* act;                 // [B][1024] residual after attention
     float* qkv;                 // [B][4096]
-    float* attn;                // [B][2048]
-    float* mlp;                 // [B][3072]
+    uint8_t* xa_qkv;            // GEMM operands (K = 1024, 2048, 1024, 3072); xa_qkv also feeds the LM head
+    uint8_t* xa_o;
+    uint8_t* xa_gu;
+    uint8_t* xa_dn;
+    float* ss_a;                // [HT][BMAX] partial sums of squares of h (QKV / LM-head RMSNorm)
+    float* ss_b;                // [HT][BMAX] of act (post-attention RMSNorm)
     float* part;                // [B][8][MAX_SPLITS_B][PARTW]
     unsigned long long* best;   // [B]
     unsigned int* ctl;          // [0] barrier counter, [1] exit counter, [2] error code, [3] error info
@@ -73,69 +107,71 @@ struct Params {
 // ---------------------------------------------------------------------------
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
-struct GemmSmem {
-    alignas(16) __nv_bfloat16 xs[2 * BMAX * XS_STRIDE];  // hi and lo planes, viewed as [2][ntok][width + 8], 133 KB
-    alignas(16) uint8_t w[2][GROUP_ROWS * (HIDDEN + ROW_SKEW)];        // 2 x 33 KB
-};
 struct AttnSmem {
     alignas(16) uint8_t kv[NW][2 * 32 * HD * 2];   // per warp: 32 positions of K then V (16 KB)
     alignas(16) float q[NW][2][HD];
 };
 struct Smem {
     union {
-        GemmSmem g;
+        alignas(128) uint8_t ring[NR][SLOT];      // GEMM slabs; after the last MMA, the fp32 epilogue tile
         AttnSmem a;
     };
-    uint64_t wbar[2];        // weight-group copies (outside the union: phases overwrite it)
+    uint64_t full[NR];       // slab copies landed
+    uint64_t mdone[NR];      // MMAs reading the slot completed (tcgen05.commit)
     uint64_t abar[NW];       // per-warp KV chunk copies
     unsigned long long tokbest[BMAX];
-    float rstd[BMAX];        // per-sequence RMSNorm factor of the phase being staged
-    float red[NW];
+    float rstd[BMAX];        // per-sequence 1/rms of the GEMM input being consumed
+    uint32_t tmem_base;
     int abort_flag;
 };
 
 struct Ctx {
     Smem* sm;
-    const Params* P;
+    unsigned int* ctl;
+    unsigned long long budget;
+    uint32_t tmem;
     unsigned int barriers;   // grid barriers passed in this launch
+    uint32_t use[NR];        // completed uses of each ring slot (mbarrier phase)
+    uint32_t pend;           // ring slots with copies issued but not yet waited for
+    int mma_slot;            // slot of the last commit nobody waited for (-1: none)
+    uint32_t mma_par;
 };
 
 __device__ __forceinline__ bool aborted(Ctx& c) {
     if (*(volatile int*)&c.sm->abort_flag) return true;
-    if (ld_relaxed32(&c.P->ctl[2]) != 0) { *(volatile int*)&c.sm->abort_flag = 1; return true; }
+    if (ld_relaxed32(&c.ctl[2]) != 0) { *(volatile int*)&c.sm->abort_flag = 1; return true; }
     return false;
 }
 __device__ __noinline__ void fail(Ctx& c, int code, int info) {
-    if (atomicCAS(&c.P->ctl[2], 0u, (unsigned)code) == 0u) atomicExch(&c.P->ctl[3], (unsigned)info);
+    if (atomicCAS(&c.ctl[2], 0u, (unsigned)code) == 0u) atomicExch(&c.ctl[3], (unsigned)info);
     *(volatile int*)&c.sm->abort_flag = 1;
+}
+
+__device__ __forceinline__ void stamp(const Params& P, int slot) {
+    if (P.trace && threadIdx.x == 0) P.trace[(size_t)blockIdx.x * 8 * (P.L + 1) + slot] = globaltimer();
 }
 
 // Bounded grid barrier (release/acquire on a monotone counter reset per launch).
 // Returns false when any CTA has failed; the caller then leaves the step.
-__device__ __forceinline__ void stamp(const Ctx& c, int slot) {
-    if (c.P->trace && threadIdx.x == 0)
-        c.P->trace[(size_t)blockIdx.x * 8 * (c.P->L + 1) + slot] = globaltimer();
-}
-
 __device__ bool grid_barrier(Ctx& c, int where) {
-    // Shared-memory bytes written through the generic proxy in this phase may be
-    // overwritten by bulk copies (async proxy) in the next one.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // Global and shared bytes written through the generic proxy in this phase
+    // are read (or overwritten) by bulk copies -- the async proxy -- in the next.
+    asm volatile("fence.proxy.async;" ::: "memory");
     __syncthreads();
     bool ok = !*(volatile int*)&c.sm->abort_flag;
     if (threadIdx.x == 0) {
         ++c.barriers;
         const unsigned target = c.barriers * gridDim.x;
         __threadfence();
-        atomicAdd(&c.P->ctl[0], 1u);
+        atomicAdd(&c.ctl[0], 1u);
         unsigned long long t0 = globaltimer();
         for (uint32_t it = 0;; ++it) {
             unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&c.P->ctl[0]) : "memory");
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&c.ctl[0]) : "memory");
             if ((int)(v - target) >= 0) break;
             if ((it & 63) == 63) {
-                if (ld_relaxed32(&c.P->ctl[2]) != 0) { c.sm->abort_flag = 1; break; }
-                if (globaltimer() - t0 > c.P->budget_ns) { fail(c, MQ_DEV_TIMEOUT_EXCHANGE, where); break; }
+                if (ld_relaxed32(&c.ctl[2]) != 0) { c.sm->abort_flag = 1; break; }
+                if (globaltimer() - t0 > c.budget) { fail(c, MQ_DEV_TIMEOUT_EXCHANGE, where); break; }
             }
         }
     } else {
@@ -145,35 +181,10 @@ __device__ bool grid_barrier(Ctx& c, int where) {
     return ok && !*(volatile int*)&c.sm->abort_flag;
 }
 
-
-// ---------------------------------------------------------------------------
-// Tensor-core GEMM pieces: D[16 rows x 8 tokens] += W[16 x 16] * X^T[16 x 8]
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t v) {  // two signed bytes -> two bf16 (exact)
-    const float lo = (float)(int8_t)(v & 0xffu), hi = (float)(int8_t)((v >> 8) & 0xffu);
-    __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// A fragment of rows (ra, ra + 8) x k [k0, k0 + 16) from int8 rows in shared memory.
-__device__ __forceinline__ void load_a(uint32_t (&a)[4], const uint8_t* ra, const uint8_t* rb, int k0, int t) {
-    const uint16_t* pa = reinterpret_cast<const uint16_t*>(ra + k0 + 2 * t);
-    const uint16_t* pb = reinterpret_cast<const uint16_t*>(rb + k0 + 2 * t);
-    a[0] = i8x2_to_bf16x2(pa[0]);
-    a[1] = i8x2_to_bf16x2(pb[0]);
-    a[2] = i8x2_to_bf16x2(pa[4]);
-    a[3] = i8x2_to_bf16x2(pb[4]);
-}
-
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Bounded mbarrier wait; gives up early when the step is aborted.
 __device__ __forceinline__ bool mbar_wait_b(Ctx& c, uint64_t* bar, uint32_t parity, int where) {
     if (mbar_test(bar, parity)) return true;
     unsigned long long t0 = globaltimer();
@@ -181,33 +192,83 @@ __device__ __forceinline__ bool mbar_wait_b(Ctx& c, uint64_t* bar, uint32_t pari
         if (mbar_test(bar, parity)) return true;
         if ((it & 63) == 0) {
             if (aborted(c)) return false;
-            if (globaltimer() - t0 > c.P->budget_ns) { fail(c, MQ_DEV_TIMEOUT_RING, where); return false; }
+            if (globaltimer() - t0 > c.budget) { fail(c, MQ_DEV_TIMEOUT_RING, where); return false; }
         }
     }
 }
-
-// Writes 16 consecutive values (this lane's part of a 512-wide slab row) as hi/lo.
-// Staged activations: xs viewed as [2][ntok][width + 8] (plane 0 = hi, 1 = lo).
-template <int NTOK, int WIDTH>
-struct XView {
-    static constexpr int RS = WIDTH + 8;
-    static constexpr int PS = NTOK * RS;
-    static_assert(2 * PS <= 2 * BMAX * XS_STRIDE, "view exceeds the staging buffer");
-};
-template <int NTOK, int WIDTH>
-__device__ __forceinline__ void put16(Smem* sm, int b, int k0, const float (&v)[16]) {
-    using V = XView<NTOK, WIDTH>;
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-        const __nv_bfloat162 hi = __floats2bfloat162_rn(v[i], v[i + 1]);
-        const float2 hf = __bfloat1622float2(hi);
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(v[i] - hf.x, v[i + 1] - hf.y);
-        *reinterpret_cast<__nv_bfloat162*>(&sm->g.xs[b * V::RS + k0 + i]) = hi;
-        *reinterpret_cast<__nv_bfloat162*>(&sm->g.xs[V::PS + b * V::RS + k0 + i]) = lo;
-    }
+// Bounded wait used while leaving after a failure: ignores the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned long long budget) {
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_test(bar, parity))
+        if (globaltimer() - t0 > budget) return;
 }
 
-// Loads 16 fp32 values [k0, k0 + 16) of a row (4 x float4, all issued together).
+// ---------------------------------------------------------------------------
+// tcgen05 pieces
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major, no swizzle: 8 x 16 B core matrices;
+// lbo = byte distance of core matrices adjacent in K, sbo = of core matrices
+// adjacent in M/N (8-row groups); descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor, kind::f16: bf16 A and B (both K-major), fp32 D, M = 128, N.
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MROWS >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 lanes x 8 consecutive fp32 columns (this warp's lane quadrant); waits for the load.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two signed bytes -> two bf16 (exact).
+__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t v) {
+    const float lo = (float)(int8_t)(v & 0xffu), hi = (float)(int8_t)((v >> 8) & 0xffu);
+    __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Writes x[0..7] (k0 .. k0 + 7 of sequence t, k0 % 8 == 0) into an activation
+// operand: bf16 hi part at row t, bf16 lo part (x - hi) at row 64 + t.
+__device__ __forceinline__ void put_x8(uint8_t* xa, int t, int k0, const float* x) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        const float2 hf = __bfloat1622float2(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    uint8_t* col = xa + (size_t)(k0 >> 3) * XCOL;
+    *reinterpret_cast<uint4*>(col + t * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(col + (BMAX + t) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// Loads 16 fp32 values [k0, k0 + 16) of a row written by other CTAs (L2).
 __device__ __forceinline__ void load16(const float* row, int k0, float (&v)[16]) {
     const float4* r = reinterpret_cast<const float4*>(row + k0);
     float4 q[4];
@@ -216,6 +277,11 @@ __device__ __forceinline__ void load16(const float* row, int k0, float (&v)[16])
 #pragma unroll
     for (int i = 0; i < 4; ++i) { v[4 * i] = q[i].x; v[4 * i + 1] = q[i].y; v[4 * i + 2] = q[i].z; v[4 * i + 3] = q[i].w; }
 }
+__device__ __forceinline__ void store16(float* row, int k0, const float (&v)[16]) {
+    float4* r = reinterpret_cast<float4*>(row + k0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
 __device__ __forceinline__ void load16_bf16(const __nv_bfloat16* row, int k0, float (&v)[16]) {
     const uint4* r = reinterpret_cast<const uint4*>(row + k0);
     const uint4 a = __ldg(r), b = __ldg(r + 1);
@@ -223,181 +289,199 @@ __device__ __forceinline__ void load16_bf16(const __nv_bfloat16* row, int k0, fl
 #pragma unroll
     for (int i = 0; i < 8; ++i) { v[2 * i] = bf16_bits_to_f32(w[i] & 0xffffu); v[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16); }
 }
-
-// Stages slab s (columns [s*SLAB, (s+1)*SLAB)) of X = RMSNorm(row_b) * w for the
-// B sequences (rows >= B are zero); row(b) is the fp32 row of sequence b, or the
-// bf16 embedding row when emb is set.  rstd is computed at s == 0 and kept in
-// shared memory.  Lane l owns columns [16l, 16l + 16) of the slab.
-template <bool EMB, class Row>
-__device__ __forceinline__ void stage_norm_slab(Smem* sm, int B, int s, const __nv_bfloat16* w, Row row) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (s == 0) {
-        for (int b = warp; b < B; b += NW) {
-            float v0[16], v1[16];
-            if constexpr (EMB) { load16_bf16(row(b), 16 * lane, v0); load16_bf16(row(b), 512 + 16 * lane, v1); }
-            else { load16(row(b), 16 * lane, v0); load16(row(b), 512 + 16 * lane, v1); }
-            float ss = 0.f;
+// hi + lo accumulator rows of sequence t, columns [col, col + 16) of the epilogue tile.
+__device__ __forceinline__ void erow16(const float* E, int ldE, int t, int col, float (&v)[16]) {
+    const float4* a = reinterpret_cast<const float4*>(E + (size_t)t * ldE + col);
+    const float4* b = reinterpret_cast<const float4*>(E + (size_t)(BMAX + t) * ldE + col);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ss += v0[i] * v0[i] + v1[i] * v1[i];
-            ss = warp_sum(ss);
-            if (lane == 0) sm->rstd[b] = rsqrtf(ss / (float)HIDDEN + RMS_EPS);
-        }
-        __syncthreads();
+    for (int i = 0; i < 4; ++i) {
+        const float4 x = a[i], y = b[i];
+        v[4 * i] = x.x + y.x; v[4 * i + 1] = x.y + y.y; v[4 * i + 2] = x.z + y.z; v[4 * i + 3] = x.w + y.w;
     }
-    float wv[16];
-    load16_bf16(w, s * SLAB + 16 * lane, wv);
-    for (int b = warp; b < BMAX; b += NW) {
-        float v[16];
-        if (b < B) {
-            if constexpr (EMB) load16_bf16(row(b), s * SLAB + 16 * lane, v);
-            else load16(row(b), s * SLAB + 16 * lane, v);
-            const float r = sm->rstd[b];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = v[i] * r * wv[i];
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        }
-        put16<BMAX, SLAB>(sm, b, 16 * lane, v);
+}
+// 1/rms of each sequence from the 64 per-tile partial sums (fixed order).
+__device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
+    for (int t = threadIdx.x; t < B; t += NT) {
+        float s = 0.f;
+#pragma unroll 16
+        for (int j = 0; j < HT; ++j) s += __ldcg(ss + j * BMAX + t);
+        sm->rstd[t] = rsqrtf(s / (float)HIDDEN + RMS_EPS);
     }
 }
 
-// LM head: X = RMSNorm(h[n0 + i]) * w for 32 tokens, full width (lane owns
-// columns [32 lane, 32 lane + 32)).
-__device__ __forceinline__ void stage_norm_half(Smem* sm, int B, int n0, const float* h, const __nv_bfloat16* w) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float w0[16], w1[16];
-    load16_bf16(w, 32 * lane, w0);
-    load16_bf16(w, 32 * lane + 16, w1);
-    for (int i = warp; i < 32; i += NW) {
-        const int b = n0 + i;
-        float v0[16], v1[16];
-        if (b < B) {
-            load16(h + (size_t)b * HIDDEN, 32 * lane, v0);
-            load16(h + (size_t)b * HIDDEN, 32 * lane + 16, v1);
-            float ss = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) ss += v0[k] * v0[k] + v1[k] * v1[k];
-            ss = warp_sum(ss);
-            const float r = rsqrtf(ss / (float)HIDDEN + RMS_EPS);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) { v0[k] *= r * w0[k]; v1[k] *= r * w1[k]; }
-        } else {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) v0[k] = v1[k] = 0.f;
-        }
-        put16<32, HIDDEN>(sm, i, 32 * lane, v0);
-        put16<32, HIDDEN>(sm, i, 32 * lane + 16, v1);
-    }
-}
-
-// Stages slab s of an fp32 [B][K] global matrix.
-__device__ __forceinline__ void stage_copy(Smem* sm, int B, const float* src, int K, int s) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < BMAX; b += NW) {
-        float v[16];
-        if (b < B) load16(src + (size_t)b * K, s * SLAB + 16 * lane, v);
-        else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        }
-        put16<BMAX, SLAB>(sm, b, 16 * lane, v);
-    }
-}
-
-// Issues the bulk copy of `n` padded rows (stride rs) starting at src into w
-// buffer `buf`; thread 0 only.  Returns the bytes expected.
-__device__ __forceinline__ void load_rows(Smem* sm, int buf, const uint8_t* src, int n, int rs, int dst_row) {
-    uint8_t* dst = sm->g.w[buf] + (size_t)dst_row * rs;
-    bulk_g2s(dst, src, (uint32_t)(n * rs), &sm->wbar[buf]);
-}
-
-// One GEMM group already being copied into w[buf]: NS = K/1024 slabs, staged by
-// stage(s).  SETS = 1: plain rows (tile i = smem rows 16i..16i+15); SETS = 2:
-// gate/up (tile i: gate rows at smem 32i.., up rows at 32i+16..), two
-// accumulators per unit.  epi(row_in_group, token, value[SETS]).
-template <int K, int SETS, int NTOK = BMAX, int WIDTH = SLAB, class Stage, class Epi>
-__device__ bool gemm_group(Ctx& c, int buf, uint32_t& wuse, int rows, Stage stage, Epi epi) {
-    constexpr int NS = K / WIDTH;
-    constexpr int RS = K + ROW_SKEW;
-    constexpr int NJ = NTOK / 8;      // n-tiles
-    using V = XView<NTOK, WIDTH>;
+// ---------------------------------------------------------------------------
+// The GEMM of one CTA: D[128 x 16 nt] = X * W^T over K, tiles given by
+// tile_ptr(j) (packed tile base, j < nt).  On success the fp32 accumulator is
+// left in shared memory as E[128][ldE] (aliasing the ring) and all threads
+// have passed a barrier; the caller runs its epilogue on E and must
+// fence_proxy_async() + __syncthreads() before the ring is used again.
+// ---------------------------------------------------------------------------
+template <int KS, class TilePtr>
+__device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_ptr, const float*& E, int& ldE) {
+    using G = SlabGeom<KS>;
     Smem* sm = c.sm;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int T = (rows + 15) / 16;
-    const int nunits = T * NJ;   // <= 16 for every group here
-    // four independent accumulation chains per unit and set: (hi, lo) x (even, odd k-step)
-    float acc[2][SETS][4][4];
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-        for (int q = 0; q < SETS; ++q)
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) acc[k][q][ch][0] = acc[k][q][ch][1] = acc[k][q][ch][2] = acc[k][q][ch][3] = 0.f;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int N = nt * TROWS, S = K / KS;
+    const int BB = 2 * N * KS, BR = N * KS;
+    const uint32_t tx = (uint32_t)(G::A_BYTES + BR);
+    auto issue = [&](int s) {   // thread 0, after the slot's previous MMAs completed
+        const int slot = s % NR;
+        uint8_t* base = sm->ring[slot];
+        mbar_arrive_expect_tx(&sm->full[slot], tx);
+        bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
+        for (int j = 0; j < nt; ++j)
+            bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS, TROWS * KS,
+                     &sm->full[slot]);
+        c.pend |= 1u << slot;
+    };
+    if (tid == 0)
+        for (int s = 0; s < min(NR, S); ++s) issue(s);
+    const uint32_t idesc = idesc_bf16(N);
     bool ok = true;
-    for (int s = 0; s < NS; ++s) {
-        if (s > 0) __syncthreads();
-        stage(s);
-        __syncthreads();
-        if (s == 0) {
-            ok = mbar_wait_b(c, &sm->wbar[buf], wuse & 1, 200 + buf);
-            ++wuse;
+    for (int s = 0; s < S; ++s) {
+        const int slot = s % NR;
+        const uint32_t par = c.use[slot] & 1u;
+        const bool okt = mbar_wait_b(c, &sm->full[slot], par, 210 + slot);
+        uint8_t* base = sm->ring[slot];
+        uint8_t* bb = base + G::A_BYTES;
+        const uint8_t* raw = bb + BB;
+        if (okt) {
+            // dequantise: item (kc, n) = 8 int8 -> one 16-byte row of a core matrix
+            for (int i = tid; i < N * (KS / 8); i += NT) {
+                const int kc = i / N, n = i - kc * N;
+                const uint2 w8 = *reinterpret_cast<const uint2*>(raw + (n >> 4) * (TROWS * KS) + kc * 128 + (n & 15) * 8);
+                uint4 o;
+                o.x = i8x2_to_bf16x2(w8.x & 0xffffu);
+                o.y = i8x2_to_bf16x2(w8.x >> 16);
+                o.z = i8x2_to_bf16x2(w8.y & 0xffffu);
+                o.w = i8x2_to_bf16x2(w8.y >> 16);
+                *reinterpret_cast<uint4*>(bb + kc * (N * 16) + n * 16) = o;
+            }
         }
-        const uint8_t* w = sm->g.w[buf];
+        fence_proxy_async();   // generic writes above -> tensor-core (async proxy) reads
+        if (!__syncthreads_and(okt && ok)) { ok = false; break; }
+        c.pend &= ~(1u << slot);
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(base), b0 = smem_u32(bb);
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int u = warp + k * NW;
-            if (u >= nunits) continue;
-            const int tile = u / NJ, j = u % NJ;
-            const __nv_bfloat16* xh = sm->g.xs + (j * 8 + g) * V::RS;
-            const __nv_bfloat16* xl = xh + V::PS;
-#pragma unroll
-            for (int q = 0; q < SETS; ++q) {
-                const int base = SETS == 1 ? tile * 16 : tile * 32 + q * 16;
-                const int lim = SETS == 1 ? rows - 1 : base + 15;
-                const uint8_t* ra = w + (size_t)min(base + g, lim) * RS + (size_t)s * WIDTH;
-                const uint8_t* rb = w + (size_t)min(base + g + 8, lim) * RS + (size_t)s * WIDTH;
-#pragma unroll 2
-                for (int ks = 0; ks < WIDTH / 16; ks += 2) {
-                    uint32_t a0[4], a1[4];
-                    load_a(a0, ra, rb, ks * 16, t);
-                    load_a(a1, ra, rb, ks * 16 + 16, t);
-                    const int k0 = ks * 16 + 2 * t;
-                    mma_bf16(acc[k][q][0], a0, *reinterpret_cast<const uint32_t*>(xh + k0), *reinterpret_cast<const uint32_t*>(xh + k0 + 8));
-                    mma_bf16(acc[k][q][1], a0, *reinterpret_cast<const uint32_t*>(xl + k0), *reinterpret_cast<const uint32_t*>(xl + k0 + 8));
-                    mma_bf16(acc[k][q][2], a1, *reinterpret_cast<const uint32_t*>(xh + k0 + 16), *reinterpret_cast<const uint32_t*>(xh + k0 + 24));
-                    mma_bf16(acc[k][q][3], a1, *reinterpret_cast<const uint32_t*>(xl + k0 + 16), *reinterpret_cast<const uint32_t*>(xl + k0 + 24));
+            for (int i = 0; i < KS / 16; ++i)
+                umma_bf16(c.tmem, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128), idesc,
+                          (s | i) != 0);
+            umma_commit(&sm->mdone[slot]);
+            c.mma_slot = slot;
+            c.mma_par = par;
+            if (s + NR < S) {
+                ok = mbar_wait_b(c, &sm->mdone[slot], par, 220 + slot);
+                if (ok) {
+                    c.mma_slot = -1;
+                    issue(s + NR);
                 }
             }
         }
+        ++c.use[slot];
     }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int u = warp + k * NW;
-        if (u >= nunits) continue;
-        const int tile = u / NJ, j = u % NJ;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = tile * 16 + g + (e >= 2 ? 8 : 0);
-            const int n = j * 8 + 2 * t + (e & 1);
-            float v[SETS];
-#pragma unroll
-            for (int q = 0; q < SETS; ++q)
-                v[q] = (acc[k][q][0][e] + acc[k][q][1][e]) + (acc[k][q][2][e] + acc[k][q][3][e]);
-            if (r < rows) epi(r, n, v);
+    if (ok) {
+        // tcgen05 operations of one thread complete in order: the last commit covers all
+        const int last = (S - 1) % NR;
+        const bool okw = mbar_wait_b(c, &sm->mdone[last], (c.use[last] - 1u) & 1u, 230);
+        ok = __syncthreads_and(okw);
+        if (ok && tid == 0) c.mma_slot = -1;
+    }
+    if (!ok) return false;
+    tc_fence_after();
+    float* Ew = reinterpret_cast<float*>(sm->ring[0]);
+    ldE = N + 4;
+    const int q = warp & 3;
+    for (int c8 = warp >> 2; c8 < N / 8; c8 += NW / 4) {
+        float v[8];
+        tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), v);
+        float* dst = Ew + (size_t)(32 * q + lane) * ldE + c8 * 8;
+        *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    E = Ew;
+    return true;
+}
+
+// Runs one CTA's row tiles [T0, T1) in passes of at most MAX_TILES_PASS tiles:
+// slab width 128 when all tiles fit one ring slot (<= 4 tiles), else 64.
+// epi(E, ldE, g0, nt) consumes each pass's accumulator (tiles g0 .. g0 + nt).
+template <class TilePtr, class Epi>
+__device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePtr tile_ptr, Epi epi) {
+    const int n = T1 - T0;
+    if (n <= 0) return true;
+    const float* E = nullptr;
+    int ldE = 0;
+    bool ok = true;
+    if (n <= SlabGeom<128>::MAX_N / TROWS) {
+        ok = tc_gemm<128>(c, xa, K, n, [&](int j) { return tile_ptr(T0 + j); }, E, ldE);
+        if (ok) epi(E, ldE, T0, n);
+    } else {
+        const int passes = (n + MAX_TILES_PASS - 1) / MAX_TILES_PASS;
+        for (int p = 0; p < passes && ok; ++p) {
+            const int g0 = T0 + split_lo(n, passes, p), g1 = T0 + split_lo(n, passes, p + 1);
+            ok = tc_gemm<64>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
+            if (ok) epi(E, ldE, g0, g1 - g0);
+            fence_proxy_async();
+            __syncthreads();
         }
+        return ok;
     }
+    fence_proxy_async();
     __syncthreads();
     return ok;
 }
 
-// Copies rows [a, a + n) (padded, stride rs) of the matrix at base into w[buf]
-// at smem row dst_row; thread 0 only, after arming the barrier.
-__device__ __forceinline__ void copy_rows(Smem* sm, int buf, const void* base, int a, int n, int rs, int dst_row) {
-    if (n <= 0) return;
-    bulk_g2s(sm->g.w[buf] + (size_t)dst_row * rs, (const uint8_t*)base + (size_t)a * rs, (uint32_t)(n * rs),
-             &sm->wbar[buf]);
+// Leaving the kernel: wait (bounded) for copies and MMAs still in flight, then free TMEM.
+__device__ void drain_and_free(Ctx& c) {
+    Smem* sm = c.sm;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NR; ++s)
+            if (c.pend & (1u << s)) mbar_drain(&sm->full[s], c.use[s] & 1u, c.budget);
+        if (c.mma_slot >= 0) mbar_drain(&sm->mdone[c.mma_slot], c.mma_par, c.budget);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if ((threadIdx.x >> 5) == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(c.tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+__device__ void alloc_tmem(Ctx& c) {
+    Smem* sm = c.sm;
+    if ((threadIdx.x >> 5) == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    c.tmem = sm->tmem_base;
+}
+__device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long budget) {
+    c.sm = sm;
+    c.ctl = ctl;
+    c.budget = budget;
+    c.tmem = 0;
+    c.barriers = 0;
+    for (int i = 0; i < NR; ++i) c.use[i] = 0;
+    c.pend = 0;
+    c.mma_slot = -1;
+    c.mma_par = 0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); }
+        for (int i = 0; i < NW; ++i) mbar_init(&sm->abar[i], 1);
+        sm->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < BMAX; i += NT) sm->tokbest[i] = 0ull;
+    __syncthreads();
+    alloc_tmem(c);
 }
 
 // ---------------------------------------------------------------------------
@@ -405,7 +489,7 @@ __device__ __forceinline__ void copy_rows(Smem* sm, int buf, const void* base, i
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int nsplit_of(int pos) { return pos / SPLIT_POS + 1; }  // cache_len = pos + 1
 
-__device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s, uint32_t& ause) {
+__device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s, uint32_t& ause, bool& apend) {
     Smem* sm = c.sm;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = P.positions[b];
@@ -511,9 +595,11 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s,
             bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp]);
             bulk_g2s(buf + 32 * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp]);
         }
+        apend = true;
         const bool okw = mbar_wait_b(c, &sm->abar[warp], ause & 1, 300);
-        ++ause;
         if (!okw) return;
+        apend = false;
+        ++ause;
         chunk(n);
     }
     if (owner) {  // the current position from registers
@@ -531,7 +617,9 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s,
     if (lane == 0) { out[2 * HD] = m0; out[2 * HD + 1] = m1; out[2 * HD + 2] = l0; out[2 * HD + 3] = l1; }
 }
 
-// One warp per (sequence, q head): merge the splits into attn (bf16).
+
+// One warp per (sequence, q head): merges the splits into the O-projection
+// operand (this lane's 4 columns = half of one 8-wide k column row).
 __device__ void merge_item(const Params& P, int b, int qh) {
     const int lane = threadIdx.x & 31;
     const int kvh = qh >> 1, hh = qh & 1;
@@ -548,10 +636,23 @@ __device__ void merge_item(const Params& P, int b, int qh) {
         o[0] = fmaf(a.x, e, o[0]); o[1] = fmaf(a.y, e, o[1]); o[2] = fmaf(a.z, e, o[2]); o[3] = fmaf(a.w, e, o[3]);
     }
     const float inv = 1.f / L;
-    float* dst = P.attn + (size_t)b * QSZ + qh * HD + 4 * lane;
-    *reinterpret_cast<float4*>(dst) = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+    uint32_t hi[2], lo[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float x0 = o[2 * i] * inv, x1 = o[2 * i + 1] * inv;
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        const float2 hf = __bfloat1622float2(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    const int k0 = qh * HD + 4 * lane;
+    uint8_t* col = P.xa_o + (size_t)(k0 >> 3) * XCOL + (k0 & 7) * 2;
+    *reinterpret_cast<uint2*>(col + b * 16) = make_uint2(hi[0], hi[1]);
+    *reinterpret_cast<uint2*>(col + (BMAX + b) * 16) = make_uint2(lo[0], lo[1]);
 }
 
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // ---------------------------------------------------------------------------
 // The step kernel
@@ -559,19 +660,11 @@ __device__ void merge_item(const Params& P, int b, int qh) {
 __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem* sm = reinterpret_cast<Smem*>(smem_raw);
-    Ctx c{sm, &P, 0u};
+    Ctx c;
+    init_ctx(c, sm, P.ctl, P.budget_ns);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = gridDim.x, cta = blockIdx.x;
     const int B = P.B;
-    if (threadIdx.x == 0) {
-        mbar_init(&sm->wbar[0], 1);
-        mbar_init(&sm->wbar[1], 1);
-        for (int i = 0; i < NW; ++i) mbar_init(&sm->abar[i], 1);
-        sm->abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    for (int i = threadIdx.x; i < BMAX; i += NT) sm->tokbest[i] = 0ull;
-    __syncthreads();
     // Every CTA validates the per-sequence inputs before touching memory with them.
     for (int t = threadIdx.x; t < B; t += NT) {
         const int tok = P.tokens_in[t], pos = P.positions[t];
@@ -579,53 +672,59 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         if (pos < 0 || pos >= P.max_seq) fail(c, MQ_DEV_BAD_POSITION, t);
     }
     __syncthreads();
-    uint32_t wuse[2] = {0u, 0u};
-    uint32_t ause = 0u;   // this warp's KV-chunk barrier uses
+    uint32_t ause = 0u;      // this warp's KV-chunk barrier uses
+    bool apend = false;      // a KV-chunk copy of this warp not waited for
     bool ok = !*(volatile int*)&sm->abort_flag;
+    // ---- embedding rows -> h and the layer-0 QKV operand ----
+    if (ok) {
+        const int T0 = split_lo(HT, nb, cta), T1 = split_lo(HT, nb, cta + 1);
+        const __nv_bfloat16* nw = (const __nv_bfloat16*)P.layers[0].input_layernorm_weight;
+        for (int i = threadIdx.x; i < B * (T1 - T0); i += NT) {
+            const int t = i % B, g = T0 + i / B, row = TROWS * g;
+            float v[16], wv[16], x[16], ss = 0.f;
+            load16_bf16(P.embed + (size_t)P.tokens_in[t] * HIDDEN, row, v);
+            load16_bf16(nw, row, wv);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) { ss += v[k] * v[k]; x[k] = v[k] * wv[k]; }
+            store16(P.h + (size_t)t * HIDDEN, row, v);
+            P.ss_a[g * BMAX + t] = ss;
+            put_x8(P.xa_qkv, t, row, x);
+            put_x8(P.xa_qkv, t, row + 8, x + 8);
+        }
+    }
+    stamp(P, 0);
+    ok = grid_barrier(c, 0) && ok;
     for (int l = 0; l < P.L && ok; ++l) {
         const LayerWeights& w = P.layers[l];
         const ScalePointers& sc = P.scales[l];
         // ---- QKV ----
         {
-            constexpr int RS = HIDDEN + ROW_SKEW;
-            const int r0 = split_lo(QKV_ROWS, nb, cta), r1 = split_lo(QKV_ROWS, nb, cta + 1);
-            if (threadIdx.x == 0) {
-                fence_proxy_async();
-                mbar_arrive_expect_tx(&sm->wbar[0], (uint32_t)((r1 - r0) * RS));
-                int done = 0;
-                while (done < r1 - r0) {
-                    const int row = r0 + done;
-                    const void* base; int first, lim;
-                    if (row < QSZ) { base = w.q_proj_weight; first = 0; lim = QSZ; }
-                    else if (row < QSZ + KVSZ) { base = w.k_proj_weight; first = QSZ; lim = QSZ + KVSZ; }
-                    else { base = w.v_proj_weight; first = QSZ + KVSZ; lim = QKV_ROWS; }
-                    const int m = min(r1 - r0 - done, lim - row);
-                    copy_rows(sm, 0, base, row - first, m, RS, done);
-                    done += m;
-                }
-            }
-            auto stage = [&](int s_) {
-                const __nv_bfloat16* nw = (const __nv_bfloat16*)w.input_layernorm_weight;
-                if (l == 0) {
-                    // h = embedding rows; CTA 0 also stores them as the fp32 residual.
-                    auto row = [&](int b) { return P.embed + (size_t)P.tokens_in[b] * HIDDEN; };
-                    stage_norm_slab<true>(sm, B, s_, nw, row);
-                    if (cta == 0 && s_ == 0)
-                        for (int i = threadIdx.x; i < B * HIDDEN; i += NT)
-                            P.h[i] = __bfloat162float(P.embed[(size_t)P.tokens_in[i / HIDDEN] * HIDDEN + i % HIDDEN]);
-                } else {
-                    stage_norm_slab<false>(sm, B, s_, nw, [&](int b) { return (const float*)P.h + (size_t)b * HIDDEN; });
-                }
-            };
+            compute_rstd(sm, P.ss_a, B);
+            const int NTQ = QKV_ROWS / TROWS;
+            const int T0 = split_lo(NTQ, nb, cta), T1 = split_lo(NTQ, nb, cta + 1);
+            const int8_t* wq = (const int8_t*)w.q_proj_weight;
+            const int8_t* wk = (const int8_t*)w.k_proj_weight;
+            const int8_t* wv = (const int8_t*)w.v_proj_weight;
             const float* sq = sc.q_scale; const float* sk = sc.k_scale; const float* sv = sc.v_scale;
-            ok = gemm_group<HIDDEN, 1>(c, 0, wuse[0], r1 - r0, stage, [&](int r, int n, const float* v) {
-                if (n >= B) return;
-                const int row = r0 + r;
-                const float s_ = row < QSZ ? sq[row] : (row < QSZ + KVSZ ? sk[row - QSZ] : sv[row - QSZ - KVSZ]);
-                P.qkv[(size_t)n * QKV_ROWS + row] = v[0] * s_;
-            }) && ok;
+            auto tp = [&](int g) -> const int8_t* {
+                return g < QSZ / TROWS ? wq + (size_t)g * TROWS * HIDDEN
+                       : g < (QSZ + KVSZ) / TROWS ? wk + (size_t)(g - QSZ / TROWS) * TROWS * HIDDEN
+                                                  : wv + (size_t)(g - (QSZ + KVSZ) / TROWS) * TROWS * HIDDEN;
+            };
+            ok = tc_rows(c, P.xa_qkv, HIDDEN, T0, T1, tp, [&](const float* E, int ldE, int g0, int nt) {
+                     for (int i = threadIdx.x; i < B * nt; i += NT) {
+                         const int t = i % B, g = g0 + i / B, row = TROWS * g;
+                         float v[16];
+                         erow16(E, ldE, t, TROWS * (g - g0), v);
+                         const float* s_ = row < QSZ ? sq + row : row < QSZ + KVSZ ? sk + (row - QSZ) : sv + (row - QSZ - KVSZ);
+                         const float r = sm->rstd[t];
+#pragma unroll
+                         for (int k = 0; k < 16; ++k) v[k] = v[k] * __ldg(s_ + k) * r;
+                         store16(P.qkv + (size_t)t * QKV_ROWS, row, v);
+                     }
+                 }) && ok;
         }
-        stamp(c, l * 8 + 1);
+        stamp(P, l * 8 + 1);
         if (!grid_barrier(c, 1)) { ok = false; break; }
         // ---- attention ----
         {
@@ -633,136 +732,150 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             int item = cta * NW + warp;
             const int stride = nb * NW;
             int b = 0, base = 0;
-            while (b < B) {
-                const int cnt = NKVH * nsplit_of(P.positions[b]);
+            while (b < B && ok) {
+                const int ns = nsplit_of(P.positions[b]);
+                const int cnt = NKVH * ns;
                 while (item < base + cnt) {
                     const int r = item - base;
-                    attn_item(c, P, l, b, r / nsplit_of(P.positions[b]), r % nsplit_of(P.positions[b]), ause);
+                    attn_item(c, P, l, b, r / ns, r % ns, ause, apend);
+                    if (apend) break;
                     item += stride;
                 }
+                if (apend) break;
                 base += cnt;
                 ++b;
             }
         }
-        stamp(c, l * 8 + 2);
+        stamp(P, l * 8 + 2);
         if (!grid_barrier(c, 2)) { ok = false; break; }
         // ---- merge ----
         for (int it = cta * NW + warp; it < B * NQH; it += nb * NW) merge_item(P, it / NQH, it % NQH);
-        stamp(c, l * 8 + 3);
+        stamp(P, l * 8 + 3);
         if (!grid_barrier(c, 3)) { ok = false; break; }
-        // ---- O + residual ----
+        // ---- O + residual -> act, GU operand ----
         {
-            constexpr int K = QSZ, RS = K + ROW_SKEW;
-            const int r0 = split_lo(HIDDEN, nb, cta), r1 = split_lo(HIDDEN, nb, cta + 1);
-            if (threadIdx.x == 0) {
-                fence_proxy_async();
-                mbar_arrive_expect_tx(&sm->wbar[1], (uint32_t)((r1 - r0) * RS));
-                copy_rows(sm, 1, w.o_proj_weight, r0, r1 - r0, RS, 0);
-            }
+            const int T0 = split_lo(HT, nb, cta), T1 = split_lo(HT, nb, cta + 1);
+            const int8_t* wo = (const int8_t*)w.o_proj_weight;
+            const __nv_bfloat16* pw = (const __nv_bfloat16*)w.post_attn_layernorm_weight;
             const float* so = sc.o_scale;
-            ok = gemm_group<K, 1>(c, 1, wuse[1], r1 - r0, [&](int s_) { stage_copy(sm, B, P.attn, K, s_); },
-                                  [&](int r, int n, const float* v) {
-                                      if (n >= B) return;
-                                      const size_t i = (size_t)n * HIDDEN + r0 + r;
-                                      P.act[i] = v[0] * so[r0 + r] + __ldcg(P.h + i);
-                                  }) && ok;
+            ok = tc_rows(c, P.xa_o, QSZ, T0, T1, [&](int g) { return wo + (size_t)g * TROWS * QSZ; },
+                         [&](const float* E, int ldE, int g0, int nt) {
+                             for (int i = threadIdx.x; i < B * nt; i += NT) {
+                                 const int t = i % B, g = g0 + i / B, row = TROWS * g;
+                                 float v[16], hv[16], wv[16], x[16], ss = 0.f;
+                                 erow16(E, ldE, t, TROWS * (g - g0), v);
+                                 load16(P.h + (size_t)t * HIDDEN, row, hv);
+                                 load16_bf16(pw, row, wv);
+#pragma unroll
+                                 for (int k = 0; k < 16; ++k) {
+                                     v[k] = v[k] * __ldg(so + row + k) + hv[k];
+                                     ss += v[k] * v[k];
+                                     x[k] = v[k] * wv[k];
+                                 }
+                                 store16(P.act + (size_t)t * HIDDEN, row, v);
+                                 P.ss_b[g * BMAX + t] = ss;
+                                 put_x8(P.xa_gu, t, row, x);
+                                 put_x8(P.xa_gu, t, row + 8, x + 8);
+                             }
+                         }) && ok;
         }
-        stamp(c, l * 8 + 4);
+        stamp(P, l * 8 + 4);
         if (!grid_barrier(c, 4)) { ok = false; break; }
-        // ---- gate/up + SiLU ----
+        // ---- gate/up + SiLU -> DOWN operand ----
         {
-            constexpr int RS = HIDDEN + ROW_SKEW;
-            const int p0 = split_lo(INTER, nb, cta), p1 = split_lo(INTER, nb, cta + 1);
+            compute_rstd(sm, P.ss_b, B);
+            const int NP = INTER / TROWS;
+            const int P0 = split_lo(NP, nb, cta), np = split_lo(NP, nb, cta + 1) - P0;
+            const int8_t* wg = (const int8_t*)w.gate_proj_weight;
+            const int8_t* wu = (const int8_t*)w.up_proj_weight;
             const float* sg = sc.gate_scale; const float* su = sc.up_scale;
-            for (int gp = p0, gi = 0; gp < p1 && ok; gp += 16, ++gi) {
-                const int np = min(16, p1 - gp);
-                const int buf = gi & 1;
-                if (threadIdx.x == 0) {
-                    fence_proxy_async();
-                    mbar_arrive_expect_tx(&sm->wbar[buf], (uint32_t)(2 * np * RS));
-                    copy_rows(sm, buf, w.gate_proj_weight, gp, np, RS, 0);
-                    copy_rows(sm, buf, w.up_proj_weight, gp, np, RS, 16);
-                }
-                ok = gemm_group<HIDDEN, 2>(c, buf, wuse[buf], np,
-                                           [&](int s_) {
-                                               stage_norm_slab<false>(sm, B, s_, (const __nv_bfloat16*)w.post_attn_layernorm_weight,
-                                                                      [&](int b) { return (const float*)P.act + (size_t)b * HIDDEN; });
-                                           },
-                                           [&](int r, int n, const float* v) {
-                                               if (n >= B) return;
-                                               const int row = gp + r;
-                                               const float gd = v[0] * sg[row], ud = v[1] * su[row];
-                                               const float silu = gd / (1.0f + expf(-gd));
-                                               P.mlp[(size_t)n * INTER + row] = silu * ud;
-                                           }) && ok;
-            }
+            // tiles [0, np): gate rows, [np, 2 np): the matching up rows (one pass: np <= 2)
+            ok = tc_rows(c, P.xa_gu, HIDDEN, 0, 2 * np,
+                         [&](int j) {
+                             return j < np ? wg + (size_t)(P0 + j) * TROWS * HIDDEN
+                                           : wu + (size_t)(P0 + j - np) * TROWS * HIDDEN;
+                         },
+                         [&](const float* E, int ldE, int, int) {
+                             for (int i = threadIdx.x; i < B * np; i += NT) {
+                                 const int t = i % B, jp = i / B, row = TROWS * (P0 + jp);
+                                 float gv[16], uv[16], m[16];
+                                 erow16(E, ldE, t, TROWS * jp, gv);
+                                 erow16(E, ldE, t, TROWS * (np + jp), uv);
+                                 const float r = sm->rstd[t];
+#pragma unroll
+                                 for (int k = 0; k < 16; ++k) {
+                                     const float gd = gv[k] * __ldg(sg + row + k) * r;
+                                     const float ud = uv[k] * __ldg(su + row + k) * r;
+                                     m[k] = gd / (1.0f + expf(-gd)) * ud;
+                                 }
+                                 put_x8(P.xa_dn, t, row, m);
+                                 put_x8(P.xa_dn, t, row + 8, m + 8);
+                             }
+                         }) && ok;
         }
-        stamp(c, l * 8 + 5);
+        stamp(P, l * 8 + 5);
         if (!grid_barrier(c, 5)) { ok = false; break; }
-        // ---- down + residual -> h ----
+        // ---- down + residual -> h, next QKV (or LM-head) operand ----
         {
-            constexpr int K = INTER, RS = K + ROW_SKEW;
-            const int r0 = split_lo(HIDDEN, nb, cta), r1 = split_lo(HIDDEN, nb, cta + 1);
-            if (threadIdx.x == 0) {
-                fence_proxy_async();
-                mbar_arrive_expect_tx(&sm->wbar[0], (uint32_t)((r1 - r0) * RS));
-                copy_rows(sm, 0, w.down_proj_weight, r0, r1 - r0, RS, 0);
-            }
+            const int T0 = split_lo(HT, nb, cta), T1 = split_lo(HT, nb, cta + 1);
+            const int8_t* wd = (const int8_t*)w.down_proj_weight;
             const float* sd = sc.down_scale;
-            ok = gemm_group<K, 1>(c, 0, wuse[0], r1 - r0, [&](int s_) { stage_copy(sm, B, P.mlp, K, s_); },
-                                  [&](int r, int n, const float* v) {
-                                      if (n >= B) return;
-                                      const size_t i = (size_t)n * HIDDEN + r0 + r;
-                                      P.h[i] = __bfloat162float(__float2bfloat16_rn(v[0] * sd[r0 + r] + __ldcg(P.act + i)));
-                                  }) && ok;
+            const __nv_bfloat16* nn =
+                l + 1 < P.L ? (const __nv_bfloat16*)P.layers[l + 1].input_layernorm_weight : P.final_norm;
+            ok = tc_rows(c, P.xa_dn, INTER, T0, T1, [&](int g) { return wd + (size_t)g * TROWS * INTER; },
+                         [&](const float* E, int ldE, int g0, int nt) {
+                             for (int i = threadIdx.x; i < B * nt; i += NT) {
+                                 const int t = i % B, g = g0 + i / B, row = TROWS * g;
+                                 float v[16], av[16], wv[16], x[16], ss = 0.f;
+                                 erow16(E, ldE, t, TROWS * (g - g0), v);
+                                 load16(P.act + (size_t)t * HIDDEN, row, av);
+                                 load16_bf16(nn, row, wv);
+#pragma unroll
+                                 for (int k = 0; k < 16; ++k) {
+                                     v[k] = bf16r(v[k] * __ldg(sd + row + k) + av[k]);
+                                     ss += v[k] * v[k];
+                                     x[k] = v[k] * wv[k];
+                                 }
+                                 store16(P.h + (size_t)t * HIDDEN, row, v);
+                                 P.ss_a[g * BMAX + t] = ss;
+                                 put_x8(P.xa_qkv, t, row, x);
+                                 put_x8(P.xa_qkv, t, row + 8, x + 8);
+                             }
+                         }) && ok;
         }
-        stamp(c, l * 8 + 6);
+        stamp(P, l * 8 + 6);
         if (!grid_barrier(c, 6)) { ok = false; break; }
     }
-    // ---- final norm + LM head + per-sequence argmax ----
-    // Two halves of 32 sequences: each half's normalised activations are staged
-    // once at full width and all of this CTA's LM-head rows stream past them.
+    // ---- LM head + per-sequence argmax ----
     if (ok) {
-        constexpr int RS = HIDDEN + ROW_SKEW;
-        const int r0 = split_lo(VOCAB, nb, cta), r1 = split_lo(VOCAB, nb, cta + 1);
-        auto issue = [&](int gr0, int buf) {
-            const int n = min(GROUP_ROWS, r1 - gr0);
-            fence_proxy_async();
-            mbar_arrive_expect_tx(&sm->wbar[buf], (uint32_t)(n * RS));
-            copy_rows(sm, buf, P.lm_w, gr0, n, RS, 0);
-        };
-        const int halves = (B + 31) / 32;
-        int gi = 0;
-        for (int hf = 0; hf < halves && ok; ++hf) {
-            const int n0 = hf * 32;
-            if (threadIdx.x == 0) issue(r0, gi & 1);
-            for (int gr = r0; gr < r1 && ok; gr += GROUP_ROWS, ++gi) {
-                const int buf = gi & 1;
-                const int n = min(GROUP_ROWS, r1 - gr);
-                // the other buffer was released by the previous group's trailing barrier
-                if (threadIdx.x == 0 && gr + GROUP_ROWS < r1) issue(gr + GROUP_ROWS, buf ^ 1);
-                const bool first = gr == r0;
-                ok = gemm_group<HIDDEN, 1, 32, HIDDEN>(
-                         c, buf, wuse[buf], n,
-                         [&](int) { if (first) stage_norm_half(sm, B, n0, P.h, P.final_norm); },
-                         [&](int r, int tl, const float* v) {
-                             const int tok = n0 + tl;
-                             if (tok >= B) return;
-                             const int row = gr + r;
-                             const float lg = v[0] * P.lm_scale[row];
-                             if (P.logits) P.logits[(size_t)tok * VOCAB + row] = lg;
-                             const unsigned long long key =
-                                 (((unsigned long long)float_order_key(lg)) << 32) | (uint32_t)(~(uint32_t)row);
-                             atomicMax(&sm->tokbest[tok], key);
-                         }) && ok;
-            }
-        }
+        compute_rstd(sm, P.ss_a, B);
+        const int NTL = VOCAB / TROWS;
+        const int T0 = split_lo(NTL, nb, cta), T1 = split_lo(NTL, nb, cta + 1);
+        ok = tc_rows(c, P.xa_qkv, HIDDEN, T0, T1, [&](int g) { return P.lm_w + (size_t)g * TROWS * HIDDEN; },
+                     [&](const float* E, int ldE, int g0, int nt) {
+                         for (int i = threadIdx.x; i < B * nt; i += NT) {
+                             const int t = i % B, g = g0 + i / B, row = TROWS * g;
+                             float v[16];
+                             erow16(E, ldE, t, TROWS * (g - g0), v);
+                             const float r = sm->rstd[t];
+                             unsigned long long best = 0ull;
+#pragma unroll
+                             for (int k = 0; k < 16; ++k) {
+                                 v[k] = v[k] * __ldg(P.lm_scale + row + k) * r;
+                                 const unsigned long long key = (((unsigned long long)float_order_key(v[k])) << 32) |
+                                                                (uint32_t)(~(uint32_t)(row + k));
+                                 best = key > best ? key : best;
+                             }
+                             if (P.logits) store16(P.logits + (size_t)t * VOCAB, row, v);
+                             atomicMax(&sm->tokbest[t], best);
+                         }
+                     }) && ok;
         __syncthreads();
         for (int t = threadIdx.x; t < B; t += NT) atomicMax(&P.best[t], sm->tokbest[t]);
     }
-    stamp(c, P.L * 8 + 6);
+    stamp(P, P.L * 8 + 6);
     grid_barrier(c, 7);
-    stamp(c, P.L * 8 + 7);
+    stamp(P, P.L * 8 + 7);
     if (cta == 0) {
         const bool err = ld_relaxed32(&P.ctl[2]) != 0;
         for (int t = threadIdx.x; t < B; t += NT) {
@@ -772,6 +885,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             if (!err) P.positions[t] += 1;
         }
     }
+    if (apend && lane == 0) mbar_drain(&sm->abar[warp], ause & 1u, P.budget_ns);
+    drain_and_free(c);
     __syncthreads();
     if (threadIdx.x == 0) {  // the last CTA out resets the barrier counter for the next launch
         __threadfence();
@@ -782,7 +897,70 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             __threadfence();
         }
     }
-    (void)lane;
+}
+
+// ---------------------------------------------------------------------------
+// Standalone GEMM through the same tensor-core path (tests, benchmarks):
+// y[t][m] = scale[m] * sum_k W[m][k] * x[t][k] for t < B.
+// ---------------------------------------------------------------------------
+struct MMParams {
+    const int8_t* w;       // tile-packed [M/16][K/64] blocks
+    const float* scale;
+    const uint8_t* xa;     // activation operand (written by xpack_kernel)
+    float* y;              // [B][M]
+    unsigned int* ctl;
+    unsigned long long budget_ns;
+    int M, K, B;
+};
+
+// x fp32 [B][K] -> activation operand (hi rows t, lo rows 64 + t; rows >= B zero).
+__global__ void xpack_kernel(const float* x, uint8_t* xa, int K, int B) {
+    const int n = BMAX * (K / 8);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int t = i % BMAX, k0 = 8 * (i / BMAX);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = t < B ? x[(size_t)t * K + k0 + j] : 0.f;
+        put_x8(xa, t, k0, v);
+    }
+}
+
+__global__ void __launch_bounds__(NT, 1) matmul_kernel(const MMParams Q) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem* sm = reinterpret_cast<Smem*>(smem_raw);
+    Ctx c;
+    init_ctx(c, sm, Q.ctl, Q.budget_ns);
+    const int NTM = Q.M / TROWS;
+    const int T0 = split_lo(NTM, gridDim.x, blockIdx.x), T1 = split_lo(NTM, gridDim.x, blockIdx.x + 1);
+    tc_rows(c, Q.xa, Q.K, T0, T1, [&](int g) { return Q.w + (size_t)g * TROWS * Q.K; },
+            [&](const float* E, int ldE, int g0, int nt) {
+                for (int i = threadIdx.x; i < Q.B * nt; i += NT) {
+                    const int t = i % Q.B, g = g0 + i / Q.B, row = TROWS * g;
+                    float v[16];
+                    erow16(E, ldE, t, TROWS * (g - g0), v);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] *= __ldg(Q.scale + row + k);
+                    store16(Q.y + (size_t)t * Q.M, row, v);
+                }
+            });
+    drain_and_free(c);
+}
+
+// INT8 [rows][K] (row stride src_stride bytes) -> tile-packed blocks:
+// block (tile, kb) at ((tile * K/64) + kb) * 1024, inside [8-k column][16 rows][8 bytes].
+__global__ void pack_tiles_kernel(const int8_t* src, int64_t rows, int K, int64_t src_stride, int8_t* dst) {
+    const int64_t n = rows * (K / 8);   // 8-byte units
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = i >> 7;              // 128 units per block
+        const int u = (int)(i & 127), kc = u >> 4, r = u & 15;
+        const int nkb = K / KBLK;
+        const int64_t tile = blk / nkb;
+        const int kb = (int)(blk - tile * nkb);
+        const int8_t* s = src + (tile * TROWS + r) * src_stride + kb * KBLK + kc * 8;
+        uint2 v;
+        memcpy(&v, s, 8);
+        *reinterpret_cast<uint2*>(dst + i * 8) = v;
+    }
 }
 
 
@@ -791,27 +969,49 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
 // ===========================================================================
 namespace {
 struct Layout {
-    size_t h, act, qkv, attn, mlp, part, best, ctl, total;
+    size_t ctl, best, h, act, qkv, xa_qkv, xa_o, xa_gu, xa_dn, ss_a, ss_b, part, total;
 };
 size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
 Layout layout(int B) {
     Layout L{};
     size_t o = 0;
-    L.ctl = o;  o += up256(4 * sizeof(unsigned));
-    L.best = o; o += up256((size_t)B * sizeof(unsigned long long));
-    L.h = o;    o += up256((size_t)B * HIDDEN * 4);
-    L.act = o;  o += up256((size_t)B * HIDDEN * 4);
-    L.qkv = o;  o += up256((size_t)B * QKV_ROWS * 4);
-    L.attn = o; o += up256((size_t)B * QSZ * 4);
-    L.mlp = o;  o += up256((size_t)B * INTER * 4);
-    L.part = o; o += up256((size_t)B * NKVH * MAX_SPLITS_B * PARTW * 4);
+    L.ctl = o;    o += up256(4 * sizeof(unsigned));
+    L.best = o;   o += up256((size_t)B * sizeof(unsigned long long));
+    L.h = o;      o += up256((size_t)B * HIDDEN * 4);
+    L.act = o;    o += up256((size_t)B * HIDDEN * 4);
+    L.qkv = o;    o += up256((size_t)B * QKV_ROWS * 4);
+    L.xa_qkv = o; o += up256((size_t)XCOL * (HIDDEN / 8));
+    L.xa_o = o;   o += up256((size_t)XCOL * (QSZ / 8));
+    L.xa_gu = o;  o += up256((size_t)XCOL * (HIDDEN / 8));
+    L.xa_dn = o;  o += up256((size_t)XCOL * (INTER / 8));
+    L.ss_a = o;   o += up256((size_t)HT * BMAX * 4);
+    L.ss_b = o;   o += up256((size_t)HT * BMAX * 4);
+    L.part = o;   o += up256((size_t)B * NKVH * MAX_SPLITS_B * PARTW * 4);
     L.total = o;
     return L;
 }
 constexpr int MAX_DEV = 64;
+constexpr int MIN_SMS = 96;   // GU: at most 2 gate/up tile pairs per CTA
 bool g_attr[MAX_DEV];
 int g_sms[MAX_DEV];
 bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+cudaError_t setup_device(int& dev) {
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= MAX_DEV) return cudaErrorInvalidDevice;
+    if (!g_attr[dev]) {
+        if ((e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        if ((e = cudaFuncSetAttribute(batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem))) !=
+            cudaSuccess)
+            return e;
+        if ((e = cudaFuncSetAttribute(matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem))) !=
+            cudaSuccess)
+            return e;
+        g_attr[dev] = true;
+    }
+    return cudaSuccess;
+}
 }  // namespace
 }  // namespace batch
 }  // namespace mq
@@ -824,6 +1024,55 @@ extern "C" int mq_batch_workspace_bytes(int batch, size_t* bytes) {
     return 0;
 }
 
+extern "C" int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
+                                    cudaStream_t stream) {
+    using namespace batch;
+    if (!src || !dst || rows <= 0 || K <= 0) return MQ_ERR_ARG;
+    if (rows % TROWS != 0 || K % KBLK != 0 || src_row_stride < K || src_row_stride % 8 != 0) return MQ_ERR_SIZE;
+    if (((uintptr_t)src & 7u) != 0 || !al16(dst)) return MQ_ERR_ARG;
+    const int64_t units = rows * (K / 8);
+    const int grid = (int)((units + 255) / 256 < 65536 ? (units + 255) / 256 : 65536);
+    pack_tiles_kernel<<<grid, 256, 0, stream>>>(src, rows, K, src_row_stride, dst);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int mq_batch_matmul_workspace_bytes(int K, size_t* bytes) {
+    if (!bytes || (K != 1024 && K != 2048 && K != 3072)) return MQ_ERR_ARG;
+    *bytes = 256 + (size_t)batch::XCOL * (K / 8);
+    return 0;
+}
+
+extern "C" int mq_batch_matmul(const int8_t* w_tiles, const float* scale, const float* x, float* y, int M, int K,
+                               int B, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    using namespace batch;
+    if (!w_tiles || !scale || !x || !y || !workspace) return MQ_ERR_ARG;
+    if ((K != 1024 && K != 2048 && K != 3072) || M <= 0 || M % TROWS != 0 || B < 1 || B > BMAX) return MQ_ERR_SIZE;
+    if (!al16(w_tiles) || !al16(y) || !al16(workspace) || ((uintptr_t)scale & 3u)) return MQ_ERR_ARG;
+    size_t need = 0;
+    mq_batch_matmul_workspace_bytes(K, &need);
+    if (workspace_bytes < need) return MQ_ERR_SIZE;
+    int dev = 0;
+    cudaError_t e = setup_device(dev);
+    if (e != cudaSuccess) return (int)e;
+    uint8_t* ws = (uint8_t*)workspace;
+    if ((e = cudaMemsetAsync(ws, 0, 256, stream)) != cudaSuccess) return (int)e;
+    xpack_kernel<<<g_sms[dev], 256, 0, stream>>>(x, ws + 256, K, B);
+    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    MMParams Q{};
+    Q.w = w_tiles;
+    Q.scale = scale;
+    Q.xa = ws + 256;
+    Q.y = y;
+    Q.ctl = (unsigned*)ws;
+    Q.budget_ns = 2000000000ull;
+    Q.M = M;
+    Q.K = K;
+    Q.B = B;
+    const int grid = g_sms[dev] < M / TROWS ? g_sms[dev] : M / TROWS;
+    matmul_kernel<<<grid, NT, sizeof(Smem), stream>>>(Q);
+    return (int)cudaGetLastError();
+}
+
 extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t stream) {
     using namespace batch;
     if (!a || num_steps <= 0) return MQ_ERR_ARG;
@@ -834,20 +1083,15 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
         !a->lm_head_scale || !a->cos_table || !a->sin_table || !a->k_cache || !a->v_cache || !a->tokens ||
         !a->positions || !a->workspace)
         return MQ_ERR_ARG;
-    if (!al16(a->lm_head_weight) || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->workspace)) return MQ_ERR_ARG;
+    if (!al16(a->lm_head_weight) || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->workspace) ||
+        !al16(a->embed_weight) || (a->logits && !al16(a->logits)))
+        return MQ_ERR_ARG;
     const Layout Lw = layout(a->batch);
     if (a->workspace_bytes < Lw.total) return MQ_ERR_SIZE;
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    cudaError_t e = setup_device(dev);
     if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= MAX_DEV) return MQ_ERR_DEVICE;
-    if (!g_attr[dev]) {
-        if ((e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return (int)e;
-        if ((e = cudaFuncSetAttribute(batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem))) !=
-            cudaSuccess)
-            return (int)e;
-        g_attr[dev] = true;
-    }
+    if (g_sms[dev] < MIN_SMS) return MQ_ERR_DEVICE;
     uint8_t* ws = (uint8_t*)a->workspace;
     Params P{};
     P.embed = (const __nv_bfloat16*)a->embed_weight;
@@ -866,8 +1110,12 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     P.h = (float*)(ws + Lw.h);
     P.act = (float*)(ws + Lw.act);
     P.qkv = (float*)(ws + Lw.qkv);
-    P.attn = (float*)(ws + Lw.attn);
-    P.mlp = (float*)(ws + Lw.mlp);
+    P.xa_qkv = ws + Lw.xa_qkv;
+    P.xa_o = ws + Lw.xa_o;
+    P.xa_gu = ws + Lw.xa_gu;
+    P.xa_dn = ws + Lw.xa_dn;
+    P.ss_a = (float*)(ws + Lw.ss_a);
+    P.ss_b = (float*)(ws + Lw.ss_b);
     P.part = (float*)(ws + Lw.part);
     P.best = (unsigned long long*)(ws + Lw.best);
     P.ctl = (unsigned*)(ws + Lw.ctl);

@@ -9,10 +9,10 @@ from .quant import quantize_per_channel, quantize_state
 from .rope import make_rope
 from .synth import make_synthetic_state
 from .decoder import A10Decoder, A10Int8MegakernelDecoder, A10MegakernelDecoder, layer_lists
-from .batch import BatchedDecoder
+from .batch import BatchedDecoder, batch_matmul, pack_tiles
 from . import _lib
 from ._lib import MQError
 
 __all__ = ["CFG", "Qwen3Config", "quantize_per_channel", "quantize_state", "make_rope", "make_synthetic_state",
-           "A10Decoder", "A10Int8MegakernelDecoder", "A10MegakernelDecoder", "BatchedDecoder", "layer_lists",
+           "A10Decoder", "A10Int8MegakernelDecoder", "A10MegakernelDecoder", "BatchedDecoder", "batch_matmul", "pack_tiles", "layer_lists",
            "MQError"]

@@ -2,11 +2,12 @@
 each at its own position with its own KV cache, advance one token per step
 while sharing one pass over the INT8 weights (csrc/batch_kernel.cu).
 
-`BatchedDecoder` borrows the padded INT8 weight tables of an
-`A10Int8MegakernelDecoder` and owns the per-sequence state: KV caches
-[B][L][8][max_seq][128] bf16, the token and position vectors and the kernel's
-workspace -- all allocated here with torch, so the C entry point itself
-allocates nothing.
+`BatchedDecoder` takes the INT8 weights of an `A10Int8MegakernelDecoder`,
+tile-packs every matrix once (`pack_tiles`: the layout the batched kernel's
+bulk copies and tensor-core GEMMs read) and owns the per-sequence state: KV
+caches [B][L][8][max_seq][128] bf16, the token and position vectors and the
+kernel's workspace -- all allocated here with torch, so the C entry point
+itself allocates nothing.
 """
 import ctypes
 
@@ -30,11 +31,51 @@ class MQBatchArgs(ctypes.Structure):
     ]
 
 
+def pack_tiles(w):
+    """INT8 [rows, K] (rows % 16 == 0, K % 64 == 0) -> tile-packed copy (same bytes,
+    16-row x 64-column 1 KB blocks; mq_pack_weight_tiles)."""
+    if w.dtype != torch.int8 or w.dim() != 2 or not w.is_cuda or not w.is_contiguous():
+        raise ValueError("pack_tiles: contiguous CUDA int8 [rows, K] expected")
+    out = torch.empty_like(w)
+    with torch.cuda.device(w.device):
+        stream = torch.cuda.current_stream(w.device).cuda_stream
+        _lib.check(_lib.load().mq_pack_weight_tiles(ctypes.c_void_p(w.data_ptr()), w.shape[0], w.shape[1], w.shape[1],
+                                                    ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream)),
+                   "mq_pack_weight_tiles")
+    return out
+
+
+def batch_matmul(w_tiles, scale, x):
+    """y[t, m] = scale[m] * sum_k W[m, k] x[t, k] on the batched path's tensor-core GEMM.
+    w_tiles: pack_tiles(W) of an int8 [M, K]; scale fp32 [M]; x fp32 [B <= 64, K]."""
+    M, K = w_tiles.shape
+    B = x.shape[0]
+    y = torch.empty((B, M), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.mq_batch_matmul_workspace_bytes(K, ctypes.byref(nbytes)), "mq_batch_matmul_workspace_bytes")
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=x.device)
+    xc = x.contiguous()
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.check(lib.mq_batch_matmul(ctypes.c_void_p(w_tiles.data_ptr()), ctypes.c_void_p(scale.data_ptr()),
+                                       ctypes.c_void_p(xc.data_ptr()), ctypes.c_void_p(y.data_ptr()), M, K, B,
+                                       ctypes.c_void_p(ws.data_ptr()), nbytes.value, ctypes.c_void_p(stream)),
+                   "mq_batch_matmul")
+    torch.cuda.synchronize(x.device)
+    code, info = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(lib.mq_batch_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(code), ctypes.byref(info)),
+               "mq_batch_status")
+    if code.value:
+        raise _lib.MQError(f"batch_matmul: device error {code.value} at {info.value}")
+    return y
+
+
 class BatchedDecoder:
     MAX_BATCH = 64
 
     def __init__(self, weights, batch, max_seq_len):
-        """weights: an A10Int8MegakernelDecoder (its padded tables are used);
+        """weights: an A10Int8MegakernelDecoder (its INT8 matrices are tile-packed here);
         max_seq_len <= 32768 and <= the rows of its RoPE tables."""
         if not 1 <= batch <= self.MAX_BATCH:
             raise ValueError(f"batch must be in [1, {self.MAX_BATCH}]")
@@ -42,6 +83,19 @@ class BatchedDecoder:
             raise ValueError("max_seq_len out of range")
         self.w = weights
         self.device = weights.device
+        # tile-packed INT8 matrices (norm weights and q/k norms unchanged)
+        self._tiles = []
+        arr = (_lib.LayerWeights * weights.num_layers_)()
+        flat = weights.layer_weights_flat_
+        for i in range(weights.num_layers_):
+            for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
+                t = flat[i * 11 + j]
+                if t.dim() == 2:
+                    t = pack_tiles(t)
+                    self._tiles.append(t)
+                setattr(arr[i], fname, t.data_ptr())
+        self.d_layer_tiles_ = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(self.device)
+        self.lm_head_tiles_ = pack_tiles(weights.lm_head_weight_)
         self.B, self.L, self.max_seq_len = batch, weights.num_layers_, max_seq_len
         shape = (batch, self.L, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
         self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
@@ -71,8 +125,8 @@ class BatchedDecoder:
         if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (self.B, VOCAB_SIZE)):
             raise ValueError("logits must be fp32 [batch, vocab]")
         w = self.w
-        a = MQBatchArgs(w.embed_weight_.data_ptr(), w.d_layer_weights_pad_.data_ptr(), w.d_layer_scales_.data_ptr(),
-                        w.final_norm_weight_.data_ptr(), w.lm_head_pad_.data_ptr(), w.lm_head_scale_.data_ptr(),
+        a = MQBatchArgs(w.embed_weight_.data_ptr(), self.d_layer_tiles_.data_ptr(), w.d_layer_scales_.data_ptr(),
+                        w.final_norm_weight_.data_ptr(), self.lm_head_tiles_.data_ptr(), w.lm_head_scale_.data_ptr(),
                         w.cos_table_.data_ptr(), w.sin_table_.data_ptr(), self.k_cache.data_ptr(),
                         self.v_cache.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
                         self.workspace.data_ptr(), self.workspace.numel(),

@@ -79,6 +79,7 @@ class _MegakernelDecoderBase:
             dt = wdtype if len(shape) == 2 else torch.bfloat16
             _check_tensor(t, f"layer {i // 11} {nm}", dt, shape, dev)
         self._keep = [embed_weight, final_norm_weight, lm_head, cos_table, sin_table, *layer_weights_flat]
+        self.layer_weights_flat_ = list(layer_weights_flat)
         self.embed_weight_, self.final_norm_weight_, self.lm_head_weight_ = embed_weight, final_norm_weight, lm_head
         self.cos_table_, self.sin_table_ = cos_table, sin_table
         arr = (_lib.LayerWeights * num_layers)()

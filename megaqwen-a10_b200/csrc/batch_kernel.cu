@@ -50,13 +50,14 @@ constexpr int MROWS = 128;               // MMA M: 64 hi rows + 64 lo rows
 constexpr int XCOL = MROWS * 16;         // bytes of one 8-wide k column of the activation operand
 constexpr int TROWS = 16;                // weight rows per packed tile
 constexpr int KBLK = 64;                 // k per packed 1 KB block
-constexpr int NR = 3;                    // ring slots
-constexpr int SLOT = 64 * 1024;          // bytes per ring slot
+constexpr int NR = 5;                    // ring slots at most (their size depends on the GEMM)
+constexpr int RING = 192 * 1024;         // ring bytes
+constexpr int NDQ = NW - 2;              // dequantising warps of the GEMM pipeline
 constexpr int TMEM_COLS = 256;           // fp32 accumulator columns (N <= 256)
 constexpr int MAX_TILES_PASS = TMEM_COLS / TROWS;
 constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension (sum-of-squares partials)
-constexpr int SPLIT_POS = 256;           // attention positions per warp item
-constexpr int MAX_SPLITS_B = 128;        // per sequence: max_seq <= 32768
+constexpr int ACH = 16;                  // positions per KV chunk copy
+constexpr int MAX_SPLITS_B = 130;        // partials per (sequence, KV head): 32768 / 256 + 2
 constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
 
 // Ring slot contents for slab width KS and N weight rows: activation slab
@@ -64,9 +65,10 @@ constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
 template <int KS>
 struct SlabGeom {
     static constexpr int A_BYTES = MROWS * KS * 2;
-    static constexpr int MAX_N = (SLOT - A_BYTES) / (3 * KS);
+    __device__ static int slot_bytes(int n) { return (A_BYTES + 3 * n * KS + 1023) & ~1023; }
 };
-static_assert(SlabGeom<128>::MAX_N >= 64 && SlabGeom<64>::MAX_N >= 256, "ring slot too small");
+static_assert(3 * (MROWS * 64 * 2 + 3 * 256 * 64) <= RING, "ring too small for three N = 256 slabs");
+static_assert(2 * (MROWS * 128 * 2 + 3 * 80 * 128) <= RING, "ring too small for two N = 80 slabs");
 
 struct Params {
     // weights: INT8 matrices tile-packed (mq_pack_weight_tiles)
@@ -108,19 +110,22 @@ struct Params {
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
 struct AttnSmem {
-    alignas(16) uint8_t kv[NW][2 * 32 * HD * 2];   // per warp: 32 positions of K then V (16 KB)
+    alignas(16) uint8_t kv[NW][2][2 * ACH * HD * 2];   // per warp: two chunks of 16 positions (K then V)
     alignas(16) float q[NW][2][HD];
 };
 struct Smem {
     union {
-        alignas(128) uint8_t ring[NR][SLOT];      // GEMM slabs; after the last MMA, the fp32 epilogue tile
+        alignas(128) uint8_t ring[RING];          // GEMM slab slots; after the last MMA, the fp32 epilogue tile
         AttnSmem a;
     };
     uint64_t full[NR];       // slab copies landed
     uint64_t mdone[NR];      // MMAs reading the slot completed (tcgen05.commit)
-    uint64_t abar[NW];       // per-warp KV chunk copies
+    uint64_t deq[NR];        // slot's weights dequantised (one arrival per dequantising warp)
+    uint64_t abar[NW][2];    // per-warp KV chunk copies (two buffers)
     unsigned long long tokbest[BMAX];
     float rstd[BMAX];        // per-sequence 1/rms of the GEMM input being consumed
+    int seqoff[BMAX + 1];    // attention work split: flattened start of each sequence
+    int segq;                // and the range length per warp
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -131,8 +136,9 @@ struct Ctx {
     unsigned long long budget;
     uint32_t tmem;
     unsigned int barriers;   // grid barriers passed in this launch
-    uint32_t use[NR];        // completed uses of each ring slot (mbarrier phase)
-    uint32_t pend;           // ring slots with copies issued but not yet waited for
+    uint32_t upar;           // bit i: parity of the next use of ring slot i (mbarrier phase)
+    uint32_t pend;           // ring slots with copies issued and not known complete (producer)
+    uint32_t ppar;           // bit i: parity of the last copy issued into slot i
     int mma_slot;            // slot of the last commit nobody waited for (-1: none)
     uint32_t mma_par;
 };
@@ -220,7 +226,7 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
 __device__ __forceinline__ uint32_t idesc_bf16(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MROWS >> 4) << 24);
 }
-__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+__device__ __forceinline__ void umma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
@@ -311,11 +317,23 @@ __device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
 
 // ---------------------------------------------------------------------------
 // The GEMM of one CTA: D[128 x 16 nt] = X * W^T over K, tiles given by
-// tile_ptr(j) (packed tile base, j < nt).  On success the fp32 accumulator is
-// left in shared memory as E[128][ldE] (aliasing the ring) and all threads
-// have passed a barrier; the caller runs its epilogue on E and must
-// fence_proxy_async() + __syncthreads() before the ring is used again.
+// tile_ptr(j) (packed tile base, j < nt).  Warp-specialised pipeline over the
+// K slabs, linked by mbarriers (no CTA-wide barrier per slab):
+//   warp 0 lane 0   producer: bulk copies of slab s into slot s % nr once the
+//                   MMAs of slab s - nr have completed (mdone);
+//   warp 1 lane 0   MMA issuer: waits for the slot's copies (full) and
+//                   dequantised weights (deq), issues the tcgen05.mma
+//                   instructions, commits to mdone;
+//   warps 2 .. 11   dequantisers: wait for the copies (full), INT8 -> 16-bit
+//                   float into the slot's operand area, one arrival per warp on deq.
+// On success the fp32 accumulator is left in shared memory as E[rows][ldE]
+// (aliasing the ring) and all threads have passed a barrier; the caller runs
+// its epilogue on E and must fence_proxy_async() + __syncthreads() before the
+// ring is used again.
 // ---------------------------------------------------------------------------
+#define IDESC(n) idesc_bf16(n)
+#define I8X2(v) i8x2_to_bf16x2(v)
+#define EQ 4
 template <int KS, class TilePtr>
 __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_ptr, const float*& E, int& ldE) {
     using G = SlabGeom<KS>;
@@ -324,76 +342,96 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     const int N = nt * TROWS, S = K / KS;
     const int BB = 2 * N * KS, BR = N * KS;
     const uint32_t tx = (uint32_t)(G::A_BYTES + BR);
-    auto issue = [&](int s) {   // thread 0, after the slot's previous MMAs completed
-        const int slot = s % NR;
-        uint8_t* base = sm->ring[slot];
-        mbar_arrive_expect_tx(&sm->full[slot], tx);
-        bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
-        for (int j = 0; j < nt; ++j)
-            bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS, TROWS * KS,
-                     &sm->full[slot]);
-        c.pend |= 1u << slot;
-    };
-    if (tid == 0)
-        for (int s = 0; s < min(NR, S); ++s) issue(s);
-    const uint32_t idesc = idesc_bf16(N);
+    const int SB = G::slot_bytes(N);
+    const int nr = min(NR, RING / SB);
+    const uint32_t par0 = c.upar;   // parity of the next use of each slot
     bool ok = true;
-    for (int s = 0; s < S; ++s) {
-        const int slot = s % NR;
-        const uint32_t par = c.use[slot] & 1u;
-        const bool okt = mbar_wait_b(c, &sm->full[slot], par, 210 + slot);
-        uint8_t* base = sm->ring[slot];
-        uint8_t* bb = base + G::A_BYTES;
-        const uint8_t* raw = bb + BB;
-        if (okt) {
-            // dequantise: item (kc, n) = 8 int8 -> one 16-byte row of a core matrix
-            for (int i = tid; i < N * (KS / 8); i += NT) {
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t mpar = par0;
+            for (int s = 0; s < S; ++s) {
+                const int slot = s % nr;
+                if (s >= nr) {   // the slot's previous MMAs must have finished reading it
+                    ok = mbar_wait_b(c, &sm->mdone[slot], (mpar >> slot) & 1u, 220 + slot);
+                    mpar ^= 1u << slot;
+                    if (!ok) break;
+                }
+                uint8_t* base = sm->ring + slot * SB;
+                mbar_arrive_expect_tx(&sm->full[slot], tx);
+                bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
+                for (int j = 0; j < nt; ++j)
+                    bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
+                             TROWS * KS, &sm->full[slot]);
+                c.pend |= 1u << slot;
+                c.ppar = (c.ppar & ~(1u << slot)) | ((((par0 >> slot) ^ (uint32_t)(s / nr)) & 1u) << slot);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = IDESC(N);
+            uint32_t dpar = par0;
+            for (int s = 0; s < S; ++s) {
+                const int slot = s % nr;
+                ok = mbar_wait_b(c, &sm->full[slot], (dpar >> slot) & 1u, 250 + slot) &&   // copies landed
+                     mbar_wait_b(c, &sm->deq[slot], (dpar >> slot) & 1u, 240 + slot);     // weights dequantised
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sm->ring + slot * SB), b0 = a0 + G::A_BYTES;
+#pragma unroll
+                for (int i = 0; i < KS / 16; ++i)
+                    umma_f16(c.tmem, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128),
+                             idesc, (s | i) != 0);
+                umma_commit(&sm->mdone[slot]);
+                c.mma_slot = slot;
+                c.mma_par = (dpar >> slot) & 1u;
+                dpar ^= 1u << slot;
+            }
+        }
+    } else {
+        const int dt = tid - 64;   // 0 .. 32 * NDQ - 1
+        uint32_t fpar = par0;
+        for (int s = 0; s < S; ++s) {
+            const int slot = s % nr;
+            ok = mbar_wait_b(c, &sm->full[slot], (fpar >> slot) & 1u, 210 + slot);
+            if (!ok) break;
+            fpar ^= 1u << slot;
+            uint8_t* bb = sm->ring + slot * SB + G::A_BYTES;
+            const uint8_t* raw = bb + BB;
+            // item (kc, n): 8 int8 -> one 16-byte row of a core matrix
+            for (int i = dt; i < N * (KS / 8); i += 32 * NDQ) {
                 const int kc = i / N, n = i - kc * N;
                 const uint2 w8 = *reinterpret_cast<const uint2*>(raw + (n >> 4) * (TROWS * KS) + kc * 128 + (n & 15) * 8);
                 uint4 o;
-                o.x = i8x2_to_bf16x2(w8.x & 0xffffu);
-                o.y = i8x2_to_bf16x2(w8.x >> 16);
-                o.z = i8x2_to_bf16x2(w8.y & 0xffffu);
-                o.w = i8x2_to_bf16x2(w8.y >> 16);
+                o.x = I8X2(w8.x & 0xffffu);
+                o.y = I8X2(w8.x >> 16);
+                o.z = I8X2(w8.y & 0xffffu);
+                o.w = I8X2(w8.y >> 16);
                 *reinterpret_cast<uint4*>(bb + kc * (N * 16) + n * 16) = o;
             }
+            fence_proxy_async();   // generic writes above -> tensor-core (async proxy) reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm->deq[slot]);
         }
-        fence_proxy_async();   // generic writes above -> tensor-core (async proxy) reads
-        if (!__syncthreads_and(okt && ok)) { ok = false; break; }
-        c.pend &= ~(1u << slot);
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(base), b0 = smem_u32(bb);
-#pragma unroll
-            for (int i = 0; i < KS / 16; ++i)
-                umma_bf16(c.tmem, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128), idesc,
-                          (s | i) != 0);
-            umma_commit(&sm->mdone[slot]);
-            c.mma_slot = slot;
-            c.mma_par = par;
-            if (s + NR < S) {
-                ok = mbar_wait_b(c, &sm->mdone[slot], par, 220 + slot);
-                if (ok) {
-                    c.mma_slot = -1;
-                    issue(s + NR);
-                }
-            }
-        }
-        ++c.use[slot];
     }
+    // every slot was used u_i times in this GEMM: flip the parities of the odd ones
+    uint32_t flip = 0u;
+    for (int i = 0; i < nr; ++i)
+        if (((S / nr) + (i < S % nr ? 1 : 0)) & 1) flip |= 1u << i;
+    c.upar = par0 ^ flip;
     if (ok) {
         // tcgen05 operations of one thread complete in order: the last commit covers all
-        const int last = (S - 1) % NR;
-        const bool okw = mbar_wait_b(c, &sm->mdone[last], (c.use[last] - 1u) & 1u, 230);
-        ok = __syncthreads_and(okw);
-        if (ok && tid == 0) c.mma_slot = -1;
+        const int last = (S - 1) % nr;
+        ok = mbar_wait_b(c, &sm->mdone[last], ((c.upar >> last) & 1u) ^ 1u, 230);
     }
+    ok = __syncthreads_and(ok);
     if (!ok) return false;
+    c.pend = 0u;
+    c.mma_slot = -1;
     tc_fence_after();
-    float* Ew = reinterpret_cast<float*>(sm->ring[0]);
+    float* Ew = reinterpret_cast<float*>(sm->ring);
     ldE = N + 4;
-    const int q = warp & 3;
-    for (int c8 = warp >> 2; c8 < N / 8; c8 += NW / 4) {
+    const int q = warp & 3;   // tcgen05.ld: warp w reaches TMEM lanes 32 (w % 4) .. + 31
+    for (int c8 = q < EQ ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
         float v[8];
         tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), v);
         float* dst = Ew + (size_t)(32 * q + lane) * ldE + c8 * 8;
@@ -407,7 +445,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
 }
 
 // Runs one CTA's row tiles [T0, T1) in passes of at most MAX_TILES_PASS tiles:
-// slab width 128 when all tiles fit one ring slot (<= 4 tiles), else 64.
+// slab width 128 when all tiles fit one pass of at most 5 tiles, else 64.
 // epi(E, ldE, g0, nt) consumes each pass's accumulator (tiles g0 .. g0 + nt).
 template <class TilePtr, class Epi>
 __device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePtr tile_ptr, Epi epi) {
@@ -416,33 +454,28 @@ __device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePt
     const float* E = nullptr;
     int ldE = 0;
     bool ok = true;
-    if (n <= SlabGeom<128>::MAX_N / TROWS) {
-        ok = tc_gemm<128>(c, xa, K, n, [&](int j) { return tile_ptr(T0 + j); }, E, ldE);
-        if (ok) epi(E, ldE, T0, n);
-    } else {
-        const int passes = (n + MAX_TILES_PASS - 1) / MAX_TILES_PASS;
-        for (int p = 0; p < passes && ok; ++p) {
-            const int g0 = T0 + split_lo(n, passes, p), g1 = T0 + split_lo(n, passes, p + 1);
+    const int passes = (n + MAX_TILES_PASS - 1) / MAX_TILES_PASS;
+    for (int p = 0; p < passes && ok; ++p) {
+        const int g0 = T0 + split_lo(n, passes, p), g1 = T0 + split_lo(n, passes, p + 1);
+        if (g1 - g0 <= 5)
+            ok = tc_gemm<128>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
+        else
             ok = tc_gemm<64>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
-            if (ok) epi(E, ldE, g0, g1 - g0);
-            fence_proxy_async();
-            __syncthreads();
-        }
-        return ok;
+        if (ok) epi(E, ldE, g0, g1 - g0);
+        fence_proxy_async();
+        __syncthreads();
     }
-    fence_proxy_async();
-    __syncthreads();
     return ok;
 }
 
 // Leaving the kernel: wait (bounded) for copies and MMAs still in flight, then free TMEM.
 __device__ void drain_and_free(Ctx& c) {
     Smem* sm = c.sm;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0)   // the producer's copies
         for (int s = 0; s < NR; ++s)
-            if (c.pend & (1u << s)) mbar_drain(&sm->full[s], c.use[s] & 1u, c.budget);
-        if (c.mma_slot >= 0) mbar_drain(&sm->mdone[c.mma_slot], c.mma_par, c.budget);
-    }
+            if (c.pend & (1u << s)) mbar_drain(&sm->full[s], (c.ppar >> s) & 1u, c.budget);
+    if (threadIdx.x == 32 && c.mma_slot >= 0)   // the MMA issuer's last commit
+        mbar_drain(&sm->mdone[c.mma_slot], c.mma_par, c.budget);
     tc_fence_before();
     __syncthreads();
     if ((threadIdx.x >> 5) == 0) {
@@ -469,13 +502,14 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
     c.budget = budget;
     c.tmem = 0;
     c.barriers = 0;
-    for (int i = 0; i < NR; ++i) c.use[i] = 0;
+    c.upar = 0;
     c.pend = 0;
+    c.ppar = 0;
     c.mma_slot = -1;
     c.mma_par = 0;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); }
-        for (int i = 0; i < NW; ++i) mbar_init(&sm->abar[i], 1);
+        for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); mbar_init(&sm->deq[i], NDQ); }
+        for (int i = 0; i < NW; ++i) { mbar_init(&sm->abar[i][0], 1); mbar_init(&sm->abar[i][1], 1); }
         sm->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -487,16 +521,26 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
 // ---------------------------------------------------------------------------
 // Attention: one warp per (sequence, KV head, split)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int nsplit_of(int pos) { return pos / SPLIT_POS + 1; }  // cache_len = pos + 1
+// Work split: the (sequence, KV head, position) triples of a step, flattened
+// sequence-major as f = seqoff[b] + kvh * cache_len_b + p, are cut into equal
+// ranges of Q (a multiple of 16, >= 256) -- one range per warp of the grid.  A
+// range that crosses (b, kvh) boundaries yields one partial per piece; the piece
+// starting at f of (b, kvh) has index f / Q - F / Q, F = the flattened start of
+// (b, kvh).  Every CTA derives the same cut from the positions, so the merge
+// needs no bookkeeping.
+__device__ __forceinline__ int nseg_of(int F, int c_len, int Q) { return (F + c_len - 1) / Q - F / Q + 1; }
 
-__device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s, uint32_t& ause, bool& apend) {
+// Positions [pa, pb) of (b, kvh) -> partial s.  The piece with pb = cache_len
+// owns the current position: it writes K/V there and takes it from registers.
+__device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa, int pb, int s, uint32_t& ause,
+                          uint32_t& apend) {
     Smem* sm = c.sm;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = P.positions[b];
     const int c_len = pos + 1;
-    const int p0 = s * SPLIT_POS;
-    const bool owner = p0 + SPLIT_POS >= c_len;   // the split that holds the current position
-    const int p1 = owner ? pos : p0 + SPLIT_POS;  // cached positions [p0, p1)
+    const int p0 = pa;
+    const bool owner = pb == c_len;
+    const int p1 = owner ? pos : pb;              // cached positions [p0, p1)
     const LayerWeights& w = P.layers[l];
     const float* qkv = P.qkv + (size_t)b * QKV_ROWS;
     const __nv_bfloat16* cosr = P.cos_t + (size_t)pos * HD;
@@ -540,77 +584,93 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s,
         }
     }
     __syncwarp();
-    const float4* q0v = reinterpret_cast<const float4*>(q);
-    const float4* q1v = reinterpret_cast<const float4*>(q + HD);
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    // lane = (head hq of the pair, position pl of a 16-position chunk) for the scores;
+    // lane owns dims [4 lane, 4 lane + 4) of both heads for the output.
+    const int hq = lane >> 4, pl = lane & 15;
+    float m = -INFINITY, lsum = 0.f;          // running max / sum of this lane's head
     float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     const float scale = P.attn_scale;
-    uint8_t* buf = sm->a.kv[warp];
-    const uint16_t* kb = reinterpret_cast<const uint16_t*>(buf);
-    const uint16_t* vb = reinterpret_cast<const uint16_t*>(buf + 32 * HD * 2);
-    auto chunk = [&](int n) {
-        float s0 = -INFINITY, s1 = -INFINITY;
-        if (lane < n) {
-            const uint16_t* kr = kb + lane * HD;
-            float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+    const float4* qv = reinterpret_cast<const float4*>(q + hq * HD);
+    auto chunk = [&](const uint8_t* buf, int n) {
+        const uint16_t* kb = reinterpret_cast<const uint16_t*>(buf);
+        const uint16_t* vb = reinterpret_cast<const uint16_t*>(buf + ACH * HD * 2);
+        float sc = -INFINITY;
+        if (pl < n) {
+            const uint16_t* kr = kb + pl * HD;
+            float x0 = 0.f, x1 = 0.f;
 #pragma unroll 8
             for (int i = 0; i < HD / 4; ++i) {
-                const int d4 = (lane + i) & (HD / 4 - 1);
+                const int d4 = (pl + i) & (HD / 4 - 1);   // rotated: the 16 rows hit distinct banks
                 const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * d4);
-                const float k0 = bf16_bits_to_f32(kw.x & 0xffffu), k1 = bf16_bits_to_f32(kw.x >> 16);
-                const float k2 = bf16_bits_to_f32(kw.y & 0xffffu), k3 = bf16_bits_to_f32(kw.y >> 16);
-                const float4 qa = q0v[d4], qb = q1v[d4];
-                x0 = fmaf(qa.x, k0, x0); x1 = fmaf(qa.y, k1, x1); x0 = fmaf(qa.z, k2, x0); x1 = fmaf(qa.w, k3, x1);
-                y0 = fmaf(qb.x, k0, y0); y1 = fmaf(qb.y, k1, y1); y0 = fmaf(qb.z, k2, y0); y1 = fmaf(qb.w, k3, y1);
+                const float4 qa = qv[d4];
+                x0 = fmaf(qa.x, bf16_bits_to_f32(kw.x & 0xffffu), x0);
+                x1 = fmaf(qa.y, bf16_bits_to_f32(kw.x >> 16), x1);
+                x0 = fmaf(qa.z, bf16_bits_to_f32(kw.y & 0xffffu), x0);
+                x1 = fmaf(qa.w, bf16_bits_to_f32(kw.y >> 16), x1);
             }
-            s0 = (x0 + x1) * scale;
-            s1 = (y0 + y1) * scale;
+            sc = (x0 + x1) * scale;
         }
-        const float n0 = fmaxf(m0, warp_max(s0)), n1 = fmaxf(m1, warp_max(s1));
-        const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);
-        const float e0 = lane < n ? expf(s0 - n0) : 0.f;
-        const float e1 = lane < n ? expf(s1 - n1) : 0.f;
-        l0 = l0 * c0 + warp_sum(e0);
-        l1 = l1 * c1 + warp_sum(e1);
+        float mx = sc;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float nm = fmaxf(m, mx);
+        const float cf = expf(m - nm);
+        const float e = pl < n ? expf(sc - nm) : 0.f;
+        float es = e;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
+        lsum = lsum * cf + es;
+        m = nm;
+        const float c0 = __shfl_sync(0xffffffffu, cf, 0), c1 = __shfl_sync(0xffffffffu, cf, 16);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
         for (int p = 0; p < n; ++p) {
-            const float ep0 = __shfl_sync(0xffffffffu, e0, p), ep1 = __shfl_sync(0xffffffffu, e1, p);
+            const float ep0 = __shfl_sync(0xffffffffu, e, p), ep1 = __shfl_sync(0xffffffffu, e, 16 + p);
             const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * lane);
             const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
             const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
             a0[0] = fmaf(ep0, v0, a0[0]); a0[1] = fmaf(ep0, v1, a0[1]); a0[2] = fmaf(ep0, v2, a0[2]); a0[3] = fmaf(ep0, v3, a0[3]);
             a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
         }
-        m0 = n0;
-        m1 = n1;
     };
+    // cached positions [p0, p1) in 16-position chunks, two in flight per warp
     const size_t head = (((size_t)b * P.L + l) * NKVH + kvh) * (size_t)P.max_seq * HD;
-    for (int p = p0; p < p1; p += 32) {
-        const int n = min(32, p1 - p);
-        __syncwarp();
-        if (lane == 0) {
-            fence_proxy_async();
-            mbar_arrive_expect_tx(&sm->abar[warp], 2u * n * HD * 2);
-            bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp]);
-            bulk_g2s(buf + 32 * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp]);
-        }
-        apend = true;
-        const bool okw = mbar_wait_b(c, &sm->abar[warp], ause & 1, 300);
-        if (!okw) return;
-        apend = false;
-        ++ause;
-        chunk(n);
+    const int nch = (p1 - p0 + ACH - 1) / ACH;
+    auto issue = [&](int ci) {   // lane 0
+        const int p = p0 + ACH * ci, n = min(ACH, p1 - p);
+        uint8_t* buf = sm->a.kv[warp][ci & 1];
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&sm->abar[warp][ci & 1], 2u * n * HD * 2);
+        bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][ci & 1]);
+        bulk_g2s(buf + ACH * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][ci & 1]);
+    };
+    __syncwarp();
+    for (int ci = 0; ci < min(2, nch); ++ci) {
+        if (lane == 0) issue(ci);
+        apend |= 1u << (ci & 1);
     }
-    if (owner) {  // the current position from registers
+    for (int ci = 0; ci < nch; ++ci) {
+        const int bs = ci & 1;
+        if (!mbar_wait_b(c, &sm->abar[warp][bs], (ause >> bs) & 1u, 300)) return;
+        apend &= ~(1u << bs);
+        ause ^= 1u << bs;
+        chunk(sm->a.kv[warp][bs], min(ACH, p1 - p0 - ACH * ci));
         __syncwarp();
-        uint16_t* kw = reinterpret_cast<uint16_t*>(buf);
-        uint16_t* vw = reinterpret_cast<uint16_t*>(buf + 32 * HD * 2);
+        if (ci + 2 < nch) {
+            if (lane == 0) issue(ci + 2);
+            apend |= 1u << bs;
+        }
+    }
+    if (owner) {  // the current position from registers (both buffers are free now)
+        uint16_t* kw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0]);
+        uint16_t* vw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0] + ACH * HD * 2);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { kw[lane + 32 * j] = kcur[j]; vw[lane + 32 * j] = vcur[j]; }
         __syncwarp();
-        chunk(1);
+        chunk(sm->a.kv[warp][0], 1);
     }
+    const float m0 = __shfl_sync(0xffffffffu, m, 0), m1 = __shfl_sync(0xffffffffu, m, 16);
+    const float l0 = __shfl_sync(0xffffffffu, lsum, 0), l1 = __shfl_sync(0xffffffffu, lsum, 16);
     float* out = P.part + (((size_t)b * NKVH + kvh) * MAX_SPLITS_B + s) * PARTW;
     *reinterpret_cast<float4*>(out + 4 * lane) = make_float4(a0[0], a0[1], a0[2], a0[3]);
     *reinterpret_cast<float4*>(out + HD + 4 * lane) = make_float4(a1[0], a1[1], a1[2], a1[3]);
@@ -620,10 +680,11 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int s,
 
 // One warp per (sequence, q head): merges the splits into the O-projection
 // operand (this lane's 4 columns = half of one 8-wide k column row).
-__device__ void merge_item(const Params& P, int b, int qh) {
+__device__ void merge_item(const Smem* sm, const Params& P, int b, int qh) {
     const int lane = threadIdx.x & 31;
     const int kvh = qh >> 1, hh = qh & 1;
-    const int ns = nsplit_of(P.positions[b]);
+    const int c_len = P.positions[b] + 1;
+    const int ns = nseg_of(sm->seqoff[b] + kvh * c_len, c_len, sm->segq);
     const float* base = P.part + ((size_t)b * NKVH + kvh) * MAX_SPLITS_B * PARTW;
     float M = -INFINITY;
     for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * PARTW + 2 * HD + hh));
@@ -671,9 +732,18 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         if (tok < 0 || tok >= VOCAB) fail(c, MQ_DEV_BAD_TOKEN, t);
         if (pos < 0 || pos >= P.max_seq) fail(c, MQ_DEV_BAD_POSITION, t);
     }
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int t = 0; t < B; ++t) { sm->seqoff[t] = o; o += NKVH * (P.positions[t] + 1); }
+        sm->seqoff[B] = o;
+        const int W = nb * NW;
+        int q = (o + W - 1) / W;
+        q = (q + 15) & ~15;
+        sm->segq = q < 256 ? 256 : q;
+    }
     __syncthreads();
-    uint32_t ause = 0u;      // this warp's KV-chunk barrier uses
-    bool apend = false;      // a KV-chunk copy of this warp not waited for
+    uint32_t ause = 0u;      // bit i: parity of the next use of this warp's KV buffer i
+    uint32_t apend = 0u;     // buffers with a KV-chunk copy not waited for
     bool ok = !*(volatile int*)&sm->abort_flag;
     // ---- embedding rows -> h and the layer-0 QKV operand ----
     if (ok) {
@@ -728,28 +798,26 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         if (!grid_barrier(c, 1)) { ok = false; break; }
         // ---- attention ----
         {
-            // items (b, kvh, s) enumerated sequence-major
-            int item = cta * NW + warp;
-            const int stride = nb * NW;
-            int b = 0, base = 0;
-            while (b < B && ok) {
-                const int ns = nsplit_of(P.positions[b]);
-                const int cnt = NKVH * ns;
-                while (item < base + cnt) {
-                    const int r = item - base;
-                    attn_item(c, P, l, b, r / ns, r % ns, ause, apend);
-                    if (apend) break;
-                    item += stride;
-                }
+            const int Q = sm->segq, T = sm->seqoff[B];
+            int f = (cta * NW + warp) * Q;
+            const int fe = min(T, f + Q);
+            int b = 0;
+            while (f < fe) {
+                while (sm->seqoff[b + 1] <= f) ++b;
+                const int c_len = P.positions[b] + 1;
+                const int r = f - sm->seqoff[b];
+                const int kvh = r / c_len, pa = r - kvh * c_len;
+                const int pb = min(c_len, pa + (fe - f));
+                const int F = sm->seqoff[b] + kvh * c_len;
+                attn_item(c, P, l, b, kvh, pa, pb, f / Q - F / Q, ause, apend);
                 if (apend) break;
-                base += cnt;
-                ++b;
+                f += pb - pa;
             }
         }
         stamp(P, l * 8 + 2);
         if (!grid_barrier(c, 2)) { ok = false; break; }
         // ---- merge ----
-        for (int it = cta * NW + warp; it < B * NQH; it += nb * NW) merge_item(P, it / NQH, it % NQH);
+        for (int it = cta * NW + warp; it < B * NQH; it += nb * NW) merge_item(sm, P, it / NQH, it % NQH);
         stamp(P, l * 8 + 3);
         if (!grid_barrier(c, 3)) { ok = false; break; }
         // ---- O + residual -> act, GU operand ----
@@ -885,7 +953,9 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             if (!err) P.positions[t] += 1;
         }
     }
-    if (apend && lane == 0) mbar_drain(&sm->abar[warp], ause & 1u, P.budget_ns);
+    if (lane == 0)
+        for (int i = 0; i < 2; ++i)
+            if (apend & (1u << i)) mbar_drain(&sm->abar[warp][i], (ause >> i) & 1u, P.budget_ns);
     drain_and_free(c);
     __syncthreads();
     if (threadIdx.x == 0) {  // the last CTA out resets the barrier counter for the next launch
@@ -1078,7 +1148,7 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     if (!a || num_steps <= 0) return MQ_ERR_ARG;
     if (a->batch < 1 || a->batch > BMAX) return MQ_ERR_SIZE;
     if (a->num_layers < 1 || a->max_seq_len < 1) return MQ_ERR_ARG;
-    if (a->max_seq_len > MAX_SPLITS_B * SPLIT_POS) return MQ_ERR_SIZE;
+    if (a->max_seq_len > 32768) return MQ_ERR_SIZE;
     if (!a->embed_weight || !a->layer_weights || !a->scales || !a->final_norm_weight || !a->lm_head_weight ||
         !a->lm_head_scale || !a->cos_table || !a->sin_table || !a->k_cache || !a->v_cache || !a->tokens ||
         !a->positions || !a->workspace)

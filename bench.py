@@ -206,7 +206,7 @@ def run_batched(args, rank, world, dist):
     line = {"metric": "batched INT8 decode tok/s (64 sequences per GPU, positions 128..2048)",
             "value": round(world * B * K / (t_max / 1000.0), 1), "unit": "tok/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(t_max / K, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8-weights/bf16x2-activations/fp32-accum",
+            "vs_baseline": None, "dtype": "int8-weights/fp16-activations/fp32-accum",
             "data": "synthetic (seeded weights, seeded N(0,1) KV caches)",
             "config": {"workload": "config4: batched decode, 64 sequences per GPU", "global_batch": world * B,
                        "parallelism": "replicas" if world > 1 else "single"},

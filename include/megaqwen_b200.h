@@ -64,7 +64,8 @@ enum {
     MQ_DEV_TIMEOUT_EXCHANGE = 1,  /* a tagged-word exchange wait ran out */
     MQ_DEV_TIMEOUT_RING = 2,      /* a weight-ring mbarrier wait ran out */
     MQ_DEV_BAD_TOKEN = 3,         /* an input token id (device-resident) is outside [0, vocab) */
-    MQ_DEV_BAD_POSITION = 4       /* a device-resident position is outside [0, max_seq_len) */
+    MQ_DEV_BAD_POSITION = 4,      /* a device-resident position is outside [0, max_seq_len) */
+    MQ_DEV_RANGE = 5              /* batched path: an activation outside the fp16 operand range (or not finite) */
 };
 
 /*
@@ -186,9 +187,11 @@ int mq_decode_multi(
  *   - logits (optional): fp32 [batch][151936] of the last step;
  *   - max_seq_len <= 32768.
  * A device-side failure leaves tokens at -1; mq_batch_status() reads the code.
- * The GEMMs run on the tcgen05 tensor cores with bf16 operands: INT8 weights
- * are dequantised exactly to bf16 in shared memory; each activation enters as
- * two bf16 parts, hi + lo (about 16 significant bits); fp32 accumulation.
+ * The GEMMs run on the tcgen05 tensor cores with fp16 operands: INT8 weights
+ * are dequantised exactly to fp16 in shared memory; activations enter as fp16
+ * of x * 2^-s (s = 8 for RMSNorm inputs, 4 otherwise; 11 significant bits);
+ * fp32 accumulation.  A value beyond the fp16 range stops the step with
+ * MQ_DEV_RANGE.
  */
 typedef struct MQBatchArgs {
     const void* embed_weight;
@@ -234,9 +237,10 @@ int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int64_t src_row
  * The batched path's tensor-core GEMM on its own:
  * y[t][m] = scale[m] * sum_k W[m][k] * x[t][k] for t < B <= 64, W tile-packed
  * [M][K] INT8 (M % 16 == 0, K in {1024, 2048, 3072}), x fp32 [B][K], y fp32
- * [B][M]; workspace of mq_batch_matmul_workspace_bytes(K) bytes, 16-byte
- * aligned.  Asynchronous on `stream`; mq_batch_status(workspace) reads a
- * device-side timeout.
+ * [B][M] (x enters the tensor cores as fp16, |x| <= 65504); workspace of
+ * mq_batch_matmul_workspace_bytes(K) bytes, 16-byte aligned.  Asynchronous on
+ * `stream`; mq_batch_status(workspace) reads a device-side timeout or range
+ * error.
  */
 int mq_batch_matmul_workspace_bytes(int K, size_t* bytes);
 int mq_batch_matmul(const int8_t* w_tiles, const float* scale, const float* x, float* y, int M, int K, int B,

@@ -18,22 +18,21 @@
 //         batch-1 kernel), next QKV (or LM-head) operand
 // then the LM-head GEMM with a per-sequence packed argmax.
 //
-// GEMM shape.  D[128 x N] = X[128 x K] * W[N x K]^T with M = 128 rows of
-// activations: rows 0..63 hold the bf16 "hi" parts of the 64 sequences, rows
-// 64..127 the bf16 "lo" parts (x = hi + lo carries ~16 significant bits), so
-// one MMA covers both and the epilogue adds row t and row 64 + t.  N = this
-// CTA's weight rows (16-row tiles, N <= 256), K streamed in slabs through a
-// three-slot shared-memory ring fed by bulk copies:
+// GEMM shape.  D[128 x N] = X[128 x K] * W[N x K]^T: rows 0..63 of X are the
+// 64 sequences' activations as fp16 of x * 2^-s (rows 64..127 are don't-care
+// and their accumulator rows are never read), N = this CTA's weight rows
+// (16-row tiles, N <= 256), K streamed in slabs through a ring of shared-memory
+// slots fed by bulk copies:
 //   * the activation operand lives in global memory already in the tensor
-//     core's K-major no-swizzle layout (8-wide k columns of [128 rows][16 B]),
+//     core's K-major no-swizzle layout (8-wide k columns of [64 rows][16 B]),
 //     written by the producing phase's epilogue, so a slab is ONE bulk copy;
 //   * the INT8 weights are tile-packed once at load time (16 rows x 64 k per
 //     1 KB block, in [8-k column][row][8 B] order), so a slab of a tile is one
-//     bulk copy; the CTA dequantises it to bf16 (exact) in shared memory in the
+//     bulk copy; the CTA dequantises it to fp16 (exact) in shared memory in the
 //     same K-major layout and one thread issues the tcgen05.mma instructions;
-//   * the per-row weight scale (and, for RMSNorm inputs, the per-sequence
-//     1/rms) multiply the fp32 accumulator in the epilogue, read back from
-//     TMEM with tcgen05.ld.
+//   * the per-row weight scale, 2^s and, for RMSNorm inputs, the per-sequence
+//     1/rms multiply the fp32 accumulator in the epilogue, read back from TMEM
+//     with tcgen05.ld.
 // RMSNorm inputs are written as h*w (norm weight applied, 1/rms not) together
 // with per-16-row partial sums of squares; the consumer reduces the 64 partials
 // in a fixed order, so results are deterministic.
@@ -46,8 +45,15 @@ namespace batch {
 constexpr int BMAX = 64;                 // sequences per launch
 constexpr int NW = 12;                   // warps per CTA
 constexpr int NT = NW * 32;
-constexpr int MROWS = 128;               // MMA M: 64 hi rows + 64 lo rows
-constexpr int XCOL = MROWS * 16;         // bytes of one 8-wide k column of the activation operand
+constexpr int MROWS = 128;               // MMA M (rows 0..63: the sequences; 64..127 unused)
+constexpr int XCOL = BMAX * 16;          // bytes of one 8-wide k column of the activation operand
+// Activation operands are stored as fp16 of x * 2^-s (exact power-of-two
+// pre-scale, undone in the epilogue): s = 8 for RMSNorm inputs (h * w, which
+// carry the residual stream's magnitude), 4 for attention and MLP outputs.
+// |x * 2^-s| must stay below 65504; a larger (or non-finite) value stops the
+// step with MQ_DEV_RANGE instead of being rounded silently.
+constexpr float XS_NORM = 1.0f / 256.0f;
+constexpr float XS_ACT = 1.0f / 16.0f;
 constexpr int TROWS = 16;                // weight rows per packed tile
 constexpr int KBLK = 64;                 // k per packed 1 KB block
 constexpr int NR = 5;                    // ring slots at most (their size depends on the GEMM)
@@ -64,11 +70,11 @@ constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
 // (128 x KS bf16), dequantised weight slab (N x KS bf16), raw weight slab (N x KS int8).
 template <int KS>
 struct SlabGeom {
-    static constexpr int A_BYTES = MROWS * KS * 2;
+    static constexpr int A_BYTES = BMAX * KS * 2;
     __device__ static int slot_bytes(int n) { return (A_BYTES + 3 * n * KS + 1023) & ~1023; }
 };
-static_assert(3 * (MROWS * 64 * 2 + 3 * 256 * 64) <= RING, "ring too small for three N = 256 slabs");
-static_assert(2 * (MROWS * 128 * 2 + 3 * 80 * 128) <= RING, "ring too small for two N = 80 slabs");
+static_assert(3 * (BMAX * 64 * 2 + 3 * 256 * 64) <= RING, "ring too small for three N = 256 slabs");
+static_assert(2 * (BMAX * 128 * 2 + 3 * 80 * 128) <= RING, "ring too small for two N = 80 slabs");
 
 struct Params {
     // weights: INT8 matrices tile-packed (mq_pack_weight_tiles)
@@ -222,9 +228,9 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// Instruction descriptor, kind::f16: bf16 A and B (both K-major), fp32 D, M = 128, N.
-__device__ __forceinline__ uint32_t idesc_bf16(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MROWS >> 4) << 24);
+// Instruction descriptor, kind::f16: fp16 A and B (both K-major), fp32 D, M = 128, N.
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MROWS >> 4) << 24);
 }
 __device__ __forceinline__ void umma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
@@ -250,28 +256,30 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Two signed bytes -> two bf16 (exact).
-__device__ __forceinline__ uint32_t i8x2_to_bf16x2(uint32_t v) {
-    const float lo = (float)(int8_t)(v & 0xffu), hi = (float)(int8_t)((v >> 8) & 0xffu);
-    __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&r);
+// Two signed bytes -> two fp16 (exact: |v| <= 128).
+__device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t v) {
+    const __half2 h = __halves2half2(__int2half_rn((int)(int8_t)(v & 0xffu)), __int2half_rn((int)(int8_t)((v >> 8) & 0xffu)));
+    return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Writes x[0..7] (k0 .. k0 + 7 of sequence t, k0 % 8 == 0) into an activation
-// operand: bf16 hi part at row t, bf16 lo part (x - hi) at row 64 + t.
-__device__ __forceinline__ void put_x8(uint8_t* xa, int t, int k0, const float* x) {
-    uint32_t hi[4], lo[4];
+// Writes x[0..7] * sc (k0 .. k0 + 7 of sequence t, k0 % 8 == 0) into an
+// activation operand as fp16 (row t of the 8-wide k column).  Returns false if
+// a value is outside the fp16 range (or not finite).
+__device__ __forceinline__ bool put_x8(uint8_t* xa, int t, int k0, const float* x, float sc) {
+    uint32_t w[4];
+    bool ok = true;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
-        const float2 hf = __bfloat1622float2(h);
-        const __nv_bfloat162 l = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
-        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
-        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+        const float a = x[2 * i] * sc, b = x[2 * i + 1] * sc;
+        ok &= fabsf(a) <= 65504.f && fabsf(b) <= 65504.f;
+        const __half2 h = __floats2half2_rn(a, b);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    uint8_t* col = xa + (size_t)(k0 >> 3) * XCOL;
-    *reinterpret_cast<uint4*>(col + t * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(col + (BMAX + t) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(xa + (size_t)(k0 >> 3) * XCOL + t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    return ok;
+}
+__device__ __noinline__ void range_fail(unsigned* ctl, int where) {
+    if (atomicCAS(&ctl[2], 0u, (unsigned)MQ_DEV_RANGE) == 0u) atomicExch(&ctl[3], (unsigned)where);
 }
 
 // Loads 16 fp32 values [k0, k0 + 16) of a row written by other CTAs (L2).
@@ -295,14 +303,13 @@ __device__ __forceinline__ void load16_bf16(const __nv_bfloat16* row, int k0, fl
 #pragma unroll
     for (int i = 0; i < 8; ++i) { v[2 * i] = bf16_bits_to_f32(w[i] & 0xffffu); v[2 * i + 1] = bf16_bits_to_f32(w[i] >> 16); }
 }
-// hi + lo accumulator rows of sequence t, columns [col, col + 16) of the epilogue tile.
-__device__ __forceinline__ void erow16(const float* E, int ldE, int t, int col, float (&v)[16]) {
+// Accumulator row of sequence t, columns [col, col + 16) of the epilogue tile, times inv.
+__device__ __forceinline__ void erow16(const float* E, int ldE, int t, int col, float inv, float (&v)[16]) {
     const float4* a = reinterpret_cast<const float4*>(E + (size_t)t * ldE + col);
-    const float4* b = reinterpret_cast<const float4*>(E + (size_t)(BMAX + t) * ldE + col);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float4 x = a[i], y = b[i];
-        v[4 * i] = x.x + y.x; v[4 * i + 1] = x.y + y.y; v[4 * i + 2] = x.z + y.z; v[4 * i + 3] = x.w + y.w;
+        const float4 x = a[i];
+        v[4 * i] = x.x * inv; v[4 * i + 1] = x.y * inv; v[4 * i + 2] = x.z * inv; v[4 * i + 3] = x.w * inv;
     }
 }
 // 1/rms of each sequence from the 64 per-tile partial sums (fixed order).
@@ -331,9 +338,6 @@ __device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
 // its epilogue on E and must fence_proxy_async() + __syncthreads() before the
 // ring is used again.
 // ---------------------------------------------------------------------------
-#define IDESC(n) idesc_bf16(n)
-#define I8X2(v) i8x2_to_bf16x2(v)
-#define EQ 4
 template <int KS, class TilePtr>
 __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_ptr, const float*& E, int& ldE) {
     using G = SlabGeom<KS>;
@@ -368,7 +372,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = IDESC(N);
+            const uint32_t idesc = idesc_f16(N);
             uint32_t dpar = par0;
             for (int s = 0; s < S; ++s) {
                 const int slot = s % nr;
@@ -402,10 +406,10 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                 const int kc = i / N, n = i - kc * N;
                 const uint2 w8 = *reinterpret_cast<const uint2*>(raw + (n >> 4) * (TROWS * KS) + kc * 128 + (n & 15) * 8);
                 uint4 o;
-                o.x = I8X2(w8.x & 0xffffu);
-                o.y = I8X2(w8.x >> 16);
-                o.z = I8X2(w8.y & 0xffffu);
-                o.w = I8X2(w8.y >> 16);
+                o.x = i8x2_to_f16x2(w8.x & 0xffffu);
+                o.y = i8x2_to_f16x2(w8.x >> 16);
+                o.z = i8x2_to_f16x2(w8.y & 0xffffu);
+                o.w = i8x2_to_f16x2(w8.y >> 16);
                 *reinterpret_cast<uint4*>(bb + kc * (N * 16) + n * 16) = o;
             }
             fence_proxy_async();   // generic writes above -> tensor-core (async proxy) reads
@@ -430,8 +434,8 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     tc_fence_after();
     float* Ew = reinterpret_cast<float*>(sm->ring);
     ldE = N + 4;
-    const int q = warp & 3;   // tcgen05.ld: warp w reaches TMEM lanes 32 (w % 4) .. + 31
-    for (int c8 = q < EQ ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
+    const int q = warp & 3;   // tcgen05.ld: warp w reaches TMEM lanes 32 (w % 4) .. + 31; rows 0..63 only
+    for (int c8 = q < 2 ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
         float v[8];
         tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), v);
         float* dst = Ew + (size_t)(32 * q + lane) * ldE + c8 * 8;
@@ -696,21 +700,19 @@ __device__ void merge_item(const Smem* sm, const Params& P, int b, int qh) {
         const float4 a = __ldcg(reinterpret_cast<const float4*>(ps + hh * HD + 4 * lane));
         o[0] = fmaf(a.x, e, o[0]); o[1] = fmaf(a.y, e, o[1]); o[2] = fmaf(a.z, e, o[2]); o[3] = fmaf(a.w, e, o[3]);
     }
-    const float inv = 1.f / L;
-    uint32_t hi[2], lo[2];
+    const float inv = XS_ACT / L;
+    uint32_t w[2];
+    bool ok = true;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const float x0 = o[2 * i] * inv, x1 = o[2 * i + 1] * inv;
-        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-        const float2 hf = __bfloat1622float2(h);
-        const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
-        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
-        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+        ok &= fabsf(x0) <= 65504.f && fabsf(x1) <= 65504.f;
+        const __half2 h = __floats2half2_rn(x0, x1);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
     const int k0 = qh * HD + 4 * lane;
-    uint8_t* col = P.xa_o + (size_t)(k0 >> 3) * XCOL + (k0 & 7) * 2;
-    *reinterpret_cast<uint2*>(col + b * 16) = make_uint2(hi[0], hi[1]);
-    *reinterpret_cast<uint2*>(col + (BMAX + b) * 16) = make_uint2(lo[0], lo[1]);
+    *reinterpret_cast<uint2*>(P.xa_o + (size_t)(k0 >> 3) * XCOL + b * 16 + (k0 & 7) * 2) = make_uint2(w[0], w[1]);
+    if (!ok) range_fail(P.ctl, 3);
 }
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -758,8 +760,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             for (int k = 0; k < 16; ++k) { ss += v[k] * v[k]; x[k] = v[k] * wv[k]; }
             store16(P.h + (size_t)t * HIDDEN, row, v);
             P.ss_a[g * BMAX + t] = ss;
-            put_x8(P.xa_qkv, t, row, x);
-            put_x8(P.xa_qkv, t, row + 8, x + 8);
+            if (!(put_x8(P.xa_qkv, t, row, x, XS_NORM) & put_x8(P.xa_qkv, t, row + 8, x + 8, XS_NORM)))
+                range_fail(P.ctl, 0);
         }
     }
     stamp(P, 0);
@@ -785,7 +787,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                      for (int i = threadIdx.x; i < B * nt; i += NT) {
                          const int t = i % B, g = g0 + i / B, row = TROWS * g;
                          float v[16];
-                         erow16(E, ldE, t, TROWS * (g - g0), v);
+                         erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_NORM, v);
                          const float* s_ = row < QSZ ? sq + row : row < QSZ + KVSZ ? sk + (row - QSZ) : sv + (row - QSZ - KVSZ);
                          const float r = sm->rstd[t];
 #pragma unroll
@@ -831,7 +833,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                              for (int i = threadIdx.x; i < B * nt; i += NT) {
                                  const int t = i % B, g = g0 + i / B, row = TROWS * g;
                                  float v[16], hv[16], wv[16], x[16], ss = 0.f;
-                                 erow16(E, ldE, t, TROWS * (g - g0), v);
+                                 erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_ACT, v);
                                  load16(P.h + (size_t)t * HIDDEN, row, hv);
                                  load16_bf16(pw, row, wv);
 #pragma unroll
@@ -842,8 +844,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                  }
                                  store16(P.act + (size_t)t * HIDDEN, row, v);
                                  P.ss_b[g * BMAX + t] = ss;
-                                 put_x8(P.xa_gu, t, row, x);
-                                 put_x8(P.xa_gu, t, row + 8, x + 8);
+                                 if (!(put_x8(P.xa_gu, t, row, x, XS_NORM) & put_x8(P.xa_gu, t, row + 8, x + 8, XS_NORM)))
+                                     range_fail(P.ctl, 4);
                              }
                          }) && ok;
         }
@@ -867,8 +869,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                              for (int i = threadIdx.x; i < B * np; i += NT) {
                                  const int t = i % B, jp = i / B, row = TROWS * (P0 + jp);
                                  float gv[16], uv[16], m[16];
-                                 erow16(E, ldE, t, TROWS * jp, gv);
-                                 erow16(E, ldE, t, TROWS * (np + jp), uv);
+                                 erow16(E, ldE, t, TROWS * jp, 1.0f / XS_NORM, gv);
+                                 erow16(E, ldE, t, TROWS * (np + jp), 1.0f / XS_NORM, uv);
                                  const float r = sm->rstd[t];
 #pragma unroll
                                  for (int k = 0; k < 16; ++k) {
@@ -876,8 +878,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                      const float ud = uv[k] * __ldg(su + row + k) * r;
                                      m[k] = gd / (1.0f + expf(-gd)) * ud;
                                  }
-                                 put_x8(P.xa_dn, t, row, m);
-                                 put_x8(P.xa_dn, t, row + 8, m + 8);
+                                 if (!(put_x8(P.xa_dn, t, row, m, XS_ACT) & put_x8(P.xa_dn, t, row + 8, m + 8, XS_ACT)))
+                                     range_fail(P.ctl, 5);
                              }
                          }) && ok;
         }
@@ -895,7 +897,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                              for (int i = threadIdx.x; i < B * nt; i += NT) {
                                  const int t = i % B, g = g0 + i / B, row = TROWS * g;
                                  float v[16], av[16], wv[16], x[16], ss = 0.f;
-                                 erow16(E, ldE, t, TROWS * (g - g0), v);
+                                 erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_ACT, v);
                                  load16(P.act + (size_t)t * HIDDEN, row, av);
                                  load16_bf16(nn, row, wv);
 #pragma unroll
@@ -906,8 +908,8 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                  }
                                  store16(P.h + (size_t)t * HIDDEN, row, v);
                                  P.ss_a[g * BMAX + t] = ss;
-                                 put_x8(P.xa_qkv, t, row, x);
-                                 put_x8(P.xa_qkv, t, row + 8, x + 8);
+                                 if (!(put_x8(P.xa_qkv, t, row, x, XS_NORM) & put_x8(P.xa_qkv, t, row + 8, x + 8, XS_NORM)))
+                                     range_fail(P.ctl, 6);
                              }
                          }) && ok;
         }
@@ -924,7 +926,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                          for (int i = threadIdx.x; i < B * nt; i += NT) {
                              const int t = i % B, g = g0 + i / B, row = TROWS * g;
                              float v[16];
-                             erow16(E, ldE, t, TROWS * (g - g0), v);
+                             erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_NORM, v);
                              const float r = sm->rstd[t];
                              unsigned long long best = 0ull;
 #pragma unroll
@@ -983,15 +985,15 @@ struct MMParams {
     int M, K, B;
 };
 
-// x fp32 [B][K] -> activation operand (hi rows t, lo rows 64 + t; rows >= B zero).
-__global__ void xpack_kernel(const float* x, uint8_t* xa, int K, int B) {
+// x fp32 [B][K] -> activation operand (fp16 rows t < B; rows >= B zero).
+__global__ void xpack_kernel(const float* x, uint8_t* xa, int K, int B, unsigned* ctl) {
     const int n = BMAX * (K / 8);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int t = i % BMAX, k0 = 8 * (i / BMAX);
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = t < B ? x[(size_t)t * K + k0 + j] : 0.f;
-        put_x8(xa, t, k0, v);
+        if (!put_x8(xa, t, k0, v, 1.0f)) range_fail(ctl, 0);
     }
 }
 
@@ -1007,7 +1009,7 @@ __global__ void __launch_bounds__(NT, 1) matmul_kernel(const MMParams Q) {
                 for (int i = threadIdx.x; i < Q.B * nt; i += NT) {
                     const int t = i % Q.B, g = g0 + i / Q.B, row = TROWS * g;
                     float v[16];
-                    erow16(E, ldE, t, TROWS * (g - g0), v);
+                    erow16(E, ldE, t, TROWS * (g - g0), 1.0f, v);
 #pragma unroll
                     for (int k = 0; k < 16; ++k) v[k] *= __ldg(Q.scale + row + k);
                     store16(Q.y + (size_t)t * Q.M, row, v);
@@ -1126,7 +1128,7 @@ extern "C" int mq_batch_matmul(const int8_t* w_tiles, const float* scale, const 
     if (e != cudaSuccess) return (int)e;
     uint8_t* ws = (uint8_t*)workspace;
     if ((e = cudaMemsetAsync(ws, 0, 256, stream)) != cudaSuccess) return (int)e;
-    xpack_kernel<<<g_sms[dev], 256, 0, stream>>>(x, ws + 256, K, B);
+    xpack_kernel<<<g_sms[dev], 256, 0, stream>>>(x, ws + 256, K, B, (unsigned*)ws);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
     MMParams Q{};
     Q.w = w_tiles;

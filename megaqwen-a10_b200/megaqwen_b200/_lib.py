@@ -19,7 +19,7 @@ MQ_ERRORS = {
 }
 ROW_PAD = 16  # padding bytes after every weight row in the layout the decoder classes use
 MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 3: "invalid token",
-                 4: "invalid position"}
+                 4: "invalid position", 5: "activation outside the fp16 operand range"}
 
 EXPORTED = (
     "launch_a10_int8_decode", "launch_a10_decode", "mq_decode_multi", "mq_quantize_per_channel",

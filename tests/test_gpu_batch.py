@@ -3,7 +3,7 @@
 Each batched step is compared sequence by sequence with a batch-1 step fed
 exactly the same input: the sequence's token, position and KV cache (copied
 from the batched state before the step).  The batched path rounds activations
-to bf16 at the tensor-core GEMM inputs (the batch-1 path keeps fp32), so the
+to fp16 at the tensor-core GEMM inputs (the batch-1 path keeps fp32), so the
 bar is the north-star per-output tolerance: logits rel_err <= 1e-2 and
 cosine >= 0.9998, the K/V written for the step to cosine >= 0.9998, and
 >= 95 % equal argmax tokens.

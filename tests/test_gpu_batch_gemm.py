@@ -2,9 +2,9 @@
 own, against a plain PyTorch fp32 reference of the same op:
 y[t, m] = scale[m] * sum_k W[m, k] x[t, k] with INT8 W tile-packed.
 
-The kernel feeds x as two bf16 parts (hi + lo, ~16 significant bits) and the
-exactly dequantised W to the tensor cores with fp32 accumulation, so the bar is
-rel_err <= 2e-4 over the output (and cosine >= 0.99999).  Shapes: every
+The kernel feeds x as fp16 (11 significant bits) and the exactly dequantised
+W to the tensor cores with fp32 accumulation, so the bar is rel_err <= 1e-3
+over the output (and cosine >= 0.9999995).  Shapes: every
 projection of the model (one tile to four per CTA, slab width 128) and the LM
 head (multi-pass, slab width 64), full and ragged batches.
 """
@@ -33,7 +33,7 @@ def _case(M, K, B, seed):
 def test_batch_gemm_matches_fp32(M, K, B):
     y, ref = _case(M, K, B, seed=M + K + B)
     e, c = O.rel_err(ref.cpu(), y.cpu()), O.cosine(ref.cpu(), y.cpu())
-    assert e <= 2e-4 and c >= 0.99999, (e, c)
+    assert e <= 1e-3 and c >= 0.9999995, (e, c)
 
 
 def test_pack_tiles_layout():

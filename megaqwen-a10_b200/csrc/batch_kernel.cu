@@ -56,11 +56,19 @@ constexpr float XS_NORM = 1.0f / 256.0f;
 constexpr float XS_ACT = 1.0f / 16.0f;
 constexpr int TROWS = 16;                // weight rows per packed tile
 constexpr int KBLK = 64;                 // k per packed 1 KB block
-constexpr int NR = 5;                    // ring slots at most (their size depends on the GEMM)
+#ifndef MQB_NR
+#define MQB_NR 8
+#endif
+constexpr int NR = MQB_NR;               // ring slots at most (their size depends on the GEMM)
 constexpr int RING = 192 * 1024;         // ring bytes
-constexpr int NDQ = NW - 2;              // dequantising warps of the GEMM pipeline
-constexpr int TMEM_COLS = 256;           // fp32 accumulator columns (N <= 256)
-constexpr int MAX_TILES_PASS = TMEM_COLS / TROWS;
+#ifndef MQB_NMMA
+#define MQB_NMMA 2
+#endif
+constexpr int NMMA = MQB_NMMA;           // MMA-issuing threads (warps 1 .. NMMA), one accumulator each
+constexpr int NDQ = NW - 1 - NMMA;       // dequantising warps of the GEMM pipeline
+constexpr int ACC_COLS = 256;            // fp32 accumulator columns (N <= 256)
+constexpr int TMEM_COLS = NMMA == 1 ? 256 : 512;   // one accumulator per MMA issuer
+constexpr int MAX_TILES_PASS = ACC_COLS / TROWS;
 constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension (sum-of-squares partials)
 constexpr int ACH = 16;                  // positions per KV chunk copy
 constexpr int MAX_SPLITS_B = 130;        // partials per (sequence, KV head): 32768 / 256 + 2
@@ -313,8 +321,11 @@ __device__ __forceinline__ void erow16(const float* E, int ldE, int t, int col, 
     }
 }
 // 1/rms of each sequence from the 64 per-tile partial sums (fixed order).
+// Run by the dequantising warps: the producer and MMA warps start the
+// GEMM pipeline meanwhile; the result is read after the GEMM's final barrier.
 __device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
-    for (int t = threadIdx.x; t < B; t += NT) {
+    for (int t = (int)threadIdx.x - 32 * (NMMA + 1); t < B; t += NT - 32 * (NMMA + 1)) {
+        if (t < 0) break;
         float s = 0.f;
 #pragma unroll 16
         for (int j = 0; j < HT; ++j) s += __ldcg(ss + j * BMAX + t);
@@ -326,13 +337,15 @@ __device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
 // The GEMM of one CTA: D[128 x 16 nt] = X * W^T over K, tiles given by
 // tile_ptr(j) (packed tile base, j < nt).  Warp-specialised pipeline over the
 // K slabs, linked by mbarriers (no CTA-wide barrier per slab):
-//   warp 0 lane 0   producer: bulk copies of slab s into slot s % nr once the
-//                   MMAs of slab s - nr have completed (mdone);
-//   warp 1 lane 0   MMA issuer: waits for the slot's copies (full) and
-//                   dequantised weights (deq), issues the tcgen05.mma
-//                   instructions, commits to mdone;
-//   warps 2 .. 11   dequantisers: wait for the copies (full), INT8 -> 16-bit
-//                   float into the slot's operand area, one arrival per warp on deq.
+//   warp 0 lane 0    producer: bulk copies of slab s into slot s % nr once the
+//                    MMAs of slab s - nr have completed (mdone);
+//   warps 1..NMMA    lane 0: MMA issuer k takes slabs k, k + NMMA, ... into its
+//                    own TMEM accumulator (summed in the epilogue): waits for
+//                    the slot's copies (full) and dequantised weights (deq),
+//                    issues the tcgen05.mma instructions, commits to mdone.
+//                    One issuer alone could not keep up with the slab rate;
+//   other warps      dequantisers: wait for the copies (full), INT8 -> fp16
+//                    into the slot's operand area, one arrival per warp on deq.
 // On success the fp32 accumulator is left in shared memory as E[rows][ldE]
 // (aliasing the ring) and all threads have passed a barrier; the caller runs
 // its epilogue on E and must fence_proxy_async() + __syncthreads() before the
@@ -349,15 +362,15 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     const int SB = G::slot_bytes(N);
     const int nr = min(NR, RING / SB);
     const uint32_t par0 = c.upar;   // parity of the next use of each slot
+    // parity of the mbarrier phases of slab s (its slot's (s / nr)-th use in this GEMM)
+    auto par = [&](int s) { return ((par0 >> (s % nr)) ^ (uint32_t)(s / nr)) & 1u; };
     bool ok = true;
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t mpar = par0;
             for (int s = 0; s < S; ++s) {
                 const int slot = s % nr;
                 if (s >= nr) {   // the slot's previous MMAs must have finished reading it
-                    ok = mbar_wait_b(c, &sm->mdone[slot], (mpar >> slot) & 1u, 220 + slot);
-                    mpar ^= 1u << slot;
+                    ok = mbar_wait_b(c, &sm->mdone[slot], par(s - nr), 220 + slot);
                     if (!ok) break;
                 }
                 uint8_t* base = sm->ring + slot * SB;
@@ -367,38 +380,37 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                     bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
                              TROWS * KS, &sm->full[slot]);
                 c.pend |= 1u << slot;
-                c.ppar = (c.ppar & ~(1u << slot)) | ((((par0 >> slot) ^ (uint32_t)(s / nr)) & 1u) << slot);
+                c.ppar = (c.ppar & ~(1u << slot)) | (par(s) << slot);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp <= NMMA) {
+        // MMA issuer k = warp - 1 takes slabs s = k, k + NMMA, ... into accumulator k
         if (lane == 0) {
+            const int k = warp - 1;
             const uint32_t idesc = idesc_f16(N);
-            uint32_t dpar = par0;
-            for (int s = 0; s < S; ++s) {
+            const uint32_t acc = c.tmem + (uint32_t)(k * ACC_COLS);
+            for (int s = k; s < S; s += NMMA) {
                 const int slot = s % nr;
-                ok = mbar_wait_b(c, &sm->full[slot], (dpar >> slot) & 1u, 250 + slot) &&   // copies landed
-                     mbar_wait_b(c, &sm->deq[slot], (dpar >> slot) & 1u, 240 + slot);     // weights dequantised
+                ok = mbar_wait_b(c, &sm->full[slot], par(s), 250 + slot) &&   // copies landed
+                     mbar_wait_b(c, &sm->deq[slot], par(s), 240 + slot);     // weights dequantised
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(sm->ring + slot * SB), b0 = a0 + G::A_BYTES;
 #pragma unroll
                 for (int i = 0; i < KS / 16; ++i)
-                    umma_f16(c.tmem, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128),
-                             idesc, (s | i) != 0);
+                    umma_f16(acc, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128), idesc,
+                             (s >= NMMA || i != 0));
                 umma_commit(&sm->mdone[slot]);
                 c.mma_slot = slot;
-                c.mma_par = (dpar >> slot) & 1u;
-                dpar ^= 1u << slot;
+                c.mma_par = par(s);
             }
         }
     } else {
-        const int dt = tid - 64;   // 0 .. 32 * NDQ - 1
-        uint32_t fpar = par0;
+        const int dt = tid - 32 * (NMMA + 1);   // 0 .. 32 * NDQ - 1
         for (int s = 0; s < S; ++s) {
             const int slot = s % nr;
-            ok = mbar_wait_b(c, &sm->full[slot], (fpar >> slot) & 1u, 210 + slot);
+            ok = mbar_wait_b(c, &sm->full[slot], par(s), 210 + slot);
             if (!ok) break;
-            fpar ^= 1u << slot;
             uint8_t* bb = sm->ring + slot * SB + G::A_BYTES;
             const uint8_t* raw = bb + BB;
             // item (kc, n): 8 int8 -> one 16-byte row of a core matrix
@@ -422,11 +434,8 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     for (int i = 0; i < nr; ++i)
         if (((S / nr) + (i < S % nr ? 1 : 0)) & 1) flip |= 1u << i;
     c.upar = par0 ^ flip;
-    if (ok) {
-        // tcgen05 operations of one thread complete in order: the last commit covers all
-        const int last = (S - 1) % nr;
-        ok = mbar_wait_b(c, &sm->mdone[last], ((c.upar >> last) & 1u) ^ 1u, 230);
-    }
+    // each issuer's tcgen05 operations complete in order: its last commit covers all of its MMAs
+    for (int s = max(0, S - NMMA); s < S && ok; ++s) ok = mbar_wait_b(c, &sm->mdone[s % nr], par(s), 230);
     ok = __syncthreads_and(ok);
     if (!ok) return false;
     c.pend = 0u;
@@ -438,6 +447,13 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     for (int c8 = q < 2 ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
         float v[8];
         tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), v);
+#pragma unroll
+        for (int k = 1; k < NMMA; ++k) {
+            float u[8];
+            tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(k * ACC_COLS + c8 * 8), u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += u[i];
+        }
         float* dst = Ew + (size_t)(32 * q + lane) * ldE + c8 * 8;
         *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
         *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
@@ -478,7 +494,7 @@ __device__ void drain_and_free(Ctx& c) {
     if (threadIdx.x == 0)   // the producer's copies
         for (int s = 0; s < NR; ++s)
             if (c.pend & (1u << s)) mbar_drain(&sm->full[s], (c.ppar >> s) & 1u, c.budget);
-    if (threadIdx.x == 32 && c.mma_slot >= 0)   // the MMA issuer's last commit
+    if (threadIdx.x >= 32 && threadIdx.x <= 32 * NMMA && (threadIdx.x & 31) == 0 && c.mma_slot >= 0)   // the MMA issuers' last commits
         mbar_drain(&sm->mdone[c.mma_slot], c.mma_par, c.budget);
     tc_fence_before();
     __syncthreads();

@@ -174,9 +174,9 @@ int mq_decode_multi(
  * at its own position with its own KV cache, advance num_steps tokens, sharing
  * one pass over the INT8 weights per step.  The caller owns all memory: the
  * library allocates nothing on this path.
- *   - weights: INT8 projections and LM head TILE-PACKED by
- *     mq_pack_weight_tiles (LayerWeights / lm_head_weight point at the packed
- *     copies), scales fp32, norms and embedding bf16;
+ *   - weights: INT8 projections TILE-PACKED by mq_pack_weight_tiles
+ *     (LayerWeights point at the packed copies), the INT8 LM head SLAB-PACKED
+ *     by mq_pack_weight_slabs, scales fp32, norms and embedding bf16;
  *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128];
  *   - tokens: device int32 [batch]: read as this step's inputs, overwritten
  *     with the argmax outputs (so repeated steps feed back on the device);
@@ -231,6 +231,11 @@ int mq_batch_status(const void* workspace, int* code, int* info);
  * rows * K bytes, 16-byte aligned.  Asynchronous on `stream`.
  */
 int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
+                         cudaStream_t stream);
+/* Same blocks, slab-major: block (kb, tile) at byte ((kb * rows/16) + tile) * 1024,
+ * so consecutive row tiles of one 64-column slab are contiguous (the batched
+ * LM head streams many tiles per slab with one copy). */
+int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
                          cudaStream_t stream);
 
 /*

@@ -264,6 +264,20 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Four signed bytes -> four fp16 (exact).  Byte b is placed as the low mantissa
+// byte of an fp16 whose exponent makes it 1024 + (b + 128) (the ulp at 1024 is
+// 1), then 1152 is subtracted: two byte permutes and two packed subtractions.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t x = w ^ 0x80808080u;   // b + 128 as an unsigned byte
+    uint32_t a, b;
+    asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(x), "r"(0x64646464u));   // {0x64, x1, 0x64, x0}
+    asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(b) : "r"(x), "r"(0x64646464u));   // {0x64, x3, 0x64, x2}
+    const __half2 bias = __float2half2_rn(1152.0f);
+    const __half2 ra = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+    const __half2 rb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+    lo = *reinterpret_cast<const uint32_t*>(&ra);
+    hi = *reinterpret_cast<const uint32_t*>(&rb);
+}
 // Two signed bytes -> two fp16 (exact: |v| <= 128).
 __device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t v) {
     const __half2 h = __halves2half2(__int2half_rn((int)(int8_t)(v & 0xffu)), __int2half_rn((int)(int8_t)((v >> 8) & 0xffu)));
@@ -352,7 +366,8 @@ __device__ __forceinline__ void compute_rstd(Smem* sm, const float* ss, int B) {
 // ring is used again.
 // ---------------------------------------------------------------------------
 template <int KS, class TilePtr>
-__device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_ptr, const float*& E, int& ldE) {
+__device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_ptr, const float*& E, int& ldE,
+                        const int8_t* slab_base = nullptr, int slab_ntm = 0, int slab_g0 = 0) {
     using G = SlabGeom<KS>;
     Smem* sm = c.sm;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -376,9 +391,13 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                 uint8_t* base = sm->ring + slot * SB;
                 mbar_arrive_expect_tx(&sm->full[slot], tx);
                 bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
-                for (int j = 0; j < nt; ++j)
-                    bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
-                             TROWS * KS, &sm->full[slot]);
+                if (KS == KBLK && slab_ntm > 0)   // slab-major packing: the nt tiles of this slab are contiguous
+                    bulk_g2s(base + G::A_BYTES + BB, slab_base + ((size_t)s * slab_ntm + slab_g0) * (TROWS * KBLK),
+                             nt * TROWS * KBLK, &sm->full[slot]);
+                else
+                    for (int j = 0; j < nt; ++j)
+                        bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
+                                 TROWS * KS, &sm->full[slot]);
                 c.pend |= 1u << slot;
                 c.ppar = (c.ppar & ~(1u << slot)) | (par(s) << slot);
             }
@@ -407,6 +426,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
         }
     } else {
         const int dt = tid - 32 * (NMMA + 1);   // 0 .. 32 * NDQ - 1
+        const int kc0 = dt / N, n0 = dt - kc0 * N, dkc = (32 * NDQ) / N, dn = (32 * NDQ) - dkc * N;
         for (int s = 0; s < S; ++s) {
             const int slot = s % nr;
             ok = mbar_wait_b(c, &sm->full[slot], par(s), 210 + slot);
@@ -414,15 +434,16 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
             uint8_t* bb = sm->ring + slot * SB + G::A_BYTES;
             const uint8_t* raw = bb + BB;
             // item (kc, n): 8 int8 -> one 16-byte row of a core matrix
-            for (int i = dt; i < N * (KS / 8); i += 32 * NDQ) {
-                const int kc = i / N, n = i - kc * N;
+            // item i = kc * N + n walks by 32 * NDQ: (kc, n) advanced without a division
+            for (int kc = kc0, n = n0; kc < KS / 8;) {
                 const uint2 w8 = *reinterpret_cast<const uint2*>(raw + (n >> 4) * (TROWS * KS) + kc * 128 + (n & 15) * 8);
                 uint4 o;
-                o.x = i8x2_to_f16x2(w8.x & 0xffffu);
-                o.y = i8x2_to_f16x2(w8.x >> 16);
-                o.z = i8x2_to_f16x2(w8.y & 0xffffu);
-                o.w = i8x2_to_f16x2(w8.y >> 16);
+                i8x4_to_f16x4(w8.x, o.x, o.y);
+                i8x4_to_f16x4(w8.y, o.z, o.w);
                 *reinterpret_cast<uint4*>(bb + kc * (N * 16) + n * 16) = o;
+                n += dn;
+                kc += dkc;
+                if (n >= N) { n -= N; ++kc; }
             }
             fence_proxy_async();   // generic writes above -> tensor-core (async proxy) reads
             __syncwarp();
@@ -468,7 +489,8 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
 // slab width 128 when all tiles fit one pass of at most 5 tiles, else 64.
 // epi(E, ldE, g0, nt) consumes each pass's accumulator (tiles g0 .. g0 + nt).
 template <class TilePtr, class Epi>
-__device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePtr tile_ptr, Epi epi) {
+__device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePtr tile_ptr, Epi epi,
+                        const int8_t* slab_base = nullptr, int slab_ntm = 0) {
     const int n = T1 - T0;
     if (n <= 0) return true;
     const float* E = nullptr;
@@ -477,7 +499,16 @@ __device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePt
     const int passes = (n + MAX_TILES_PASS - 1) / MAX_TILES_PASS;
     for (int p = 0; p < passes && ok; ++p) {
         const int g0 = T0 + split_lo(n, passes, p), g1 = T0 + split_lo(n, passes, p + 1);
-        if (g1 - g0 <= 5)
+#ifndef MQB_KSL
+#define MQB_KSL 256
+#endif
+        if (slab_ntm > 0)
+            ok = tc_gemm<64>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE, slab_base, slab_ntm, g0);
+        else if (MQB_KSL >= 512 && SlabGeom<512>::A_BYTES + 3 * (g1 - g0) * TROWS * 512 <= RING / 2 && K % 512 == 0)
+            ok = tc_gemm<512>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
+        else if (MQB_KSL >= 256 && SlabGeom<256>::A_BYTES + 3 * (g1 - g0) * TROWS * 256 <= RING / 3)
+            ok = tc_gemm<256>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
+        else if (g1 - g0 <= 5)
             ok = tc_gemm<128>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
         else
             ok = tc_gemm<64>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
@@ -955,7 +986,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                              if (P.logits) store16(P.logits + (size_t)t * VOCAB, row, v);
                              atomicMax(&sm->tokbest[t], best);
                          }
-                     }) && ok;
+                     }, P.lm_w, NTL) && ok;
         __syncthreads();
         for (int t = threadIdx.x; t < B; t += NT) atomicMax(&P.best[t], sm->tokbest[t]);
     }
@@ -1032,6 +1063,23 @@ __global__ void __launch_bounds__(NT, 1) matmul_kernel(const MMParams Q) {
                 }
             });
     drain_and_free(c);
+}
+
+// INT8 [rows][K] -> slab-major packed blocks: block (kb, tile) at
+// ((kb * rows/16) + tile) * 1024, inside [8-k column][16 rows][8 bytes].
+__global__ void pack_slabs_kernel(const int8_t* src, int64_t rows, int K, int64_t src_stride, int8_t* dst) {
+    const int64_t n = rows * (K / 8);
+    const int64_t ntiles = rows / TROWS;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = i >> 7;
+        const int u = (int)(i & 127), kc = u >> 4, r = u & 15;
+        const int kb = (int)(blk / ntiles);
+        const int64_t tile = blk - (int64_t)kb * ntiles;
+        const int8_t* s = src + (tile * TROWS + r) * src_stride + kb * KBLK + kc * 8;
+        uint2 v;
+        memcpy(&v, s, 8);
+        *reinterpret_cast<uint2*>(dst + i * 8) = v;
+    }
 }
 
 // INT8 [rows][K] (row stride src_stride bytes) -> tile-packed blocks:
@@ -1121,6 +1169,18 @@ extern "C" int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int6
     const int64_t units = rows * (K / 8);
     const int grid = (int)((units + 255) / 256 < 65536 ? (units + 255) / 256 : 65536);
     pack_tiles_kernel<<<grid, 256, 0, stream>>>(src, rows, K, src_row_stride, dst);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
+                                    cudaStream_t stream) {
+    using namespace batch;
+    if (!src || !dst || rows <= 0 || K <= 0) return MQ_ERR_ARG;
+    if (rows % TROWS != 0 || K % KBLK != 0 || src_row_stride < K || src_row_stride % 8 != 0) return MQ_ERR_SIZE;
+    if (((uintptr_t)src & 7u) != 0 || !al16(dst)) return MQ_ERR_ARG;
+    const int64_t units = rows * (K / 8);
+    const int grid = (int)((units + 255) / 256 < 65536 ? (units + 255) / 256 : 65536);
+    pack_slabs_kernel<<<grid, 256, 0, stream>>>(src, rows, K, src_row_stride, dst);
     return (int)cudaGetLastError();
 }
 

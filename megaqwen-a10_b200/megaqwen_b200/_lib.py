@@ -25,7 +25,7 @@ EXPORTED = (
     "launch_a10_int8_decode", "launch_a10_decode", "mq_decode_multi", "mq_quantize_per_channel",
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
     "mq_set_trace", "launch_a10_int8_decode_static", "mq_batch_workspace_bytes", "mq_batch_decode",
-    "mq_batch_status", "mq_pack_weight_tiles", "mq_batch_matmul_workspace_bytes", "mq_batch_matmul",
+    "mq_batch_status", "mq_pack_weight_tiles", "mq_pack_weight_slabs", "mq_batch_matmul_workspace_bytes", "mq_batch_matmul",
 )
 
 
@@ -73,6 +73,7 @@ def load():
     lib.mq_batch_decode.argtypes = [_vp, _i, _vp]
     lib.mq_batch_status.argtypes = [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]
     lib.mq_pack_weight_tiles.argtypes = [_vp, _i64, _i, _i64, _vp, _vp]
+    lib.mq_pack_weight_slabs.argtypes = [_vp, _i64, _i, _i64, _vp, _vp]
     lib.mq_batch_matmul_workspace_bytes.argtypes = [_i, ctypes.POINTER(ctypes.c_size_t)]
     lib.mq_batch_matmul.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, ctypes.c_size_t, _vp]
     lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]

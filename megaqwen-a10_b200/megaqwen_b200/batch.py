@@ -31,17 +31,19 @@ class MQBatchArgs(ctypes.Structure):
     ]
 
 
-def pack_tiles(w):
-    """INT8 [rows, K] (rows % 16 == 0, K % 64 == 0) -> tile-packed copy (same bytes,
-    16-row x 64-column 1 KB blocks; mq_pack_weight_tiles)."""
+def pack_tiles(w, slab_major=False):
+    """INT8 [rows, K] (rows % 16 == 0, K % 64 == 0) -> packed copy (same bytes, 16-row x
+    64-column 1 KB blocks): tile-major (mq_pack_weight_tiles, the projections) or
+    slab-major (mq_pack_weight_slabs, the LM head)."""
     if w.dtype != torch.int8 or w.dim() != 2 or not w.is_cuda or not w.is_contiguous():
         raise ValueError("pack_tiles: contiguous CUDA int8 [rows, K] expected")
     out = torch.empty_like(w)
+    lib = _lib.load()
+    fn = lib.mq_pack_weight_slabs if slab_major else lib.mq_pack_weight_tiles
     with torch.cuda.device(w.device):
         stream = torch.cuda.current_stream(w.device).cuda_stream
-        _lib.check(_lib.load().mq_pack_weight_tiles(ctypes.c_void_p(w.data_ptr()), w.shape[0], w.shape[1], w.shape[1],
-                                                    ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream)),
-                   "mq_pack_weight_tiles")
+        _lib.check(fn(ctypes.c_void_p(w.data_ptr()), w.shape[0], w.shape[1], w.shape[1],
+                      ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream)), "pack_tiles")
     return out
 
 
@@ -95,7 +97,7 @@ class BatchedDecoder:
                     self._tiles.append(t)
                 setattr(arr[i], fname, t.data_ptr())
         self.d_layer_tiles_ = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(self.device)
-        self.lm_head_tiles_ = pack_tiles(weights.lm_head_weight_)
+        self.lm_head_tiles_ = pack_tiles(weights.lm_head_weight_, slab_major=True)
         self.B, self.L, self.max_seq_len = batch, weights.num_layers_, max_seq_len
         shape = (batch, self.L, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
         self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)

@@ -47,3 +47,16 @@ def test_pack_tiles_layout():
                 for r in range(16):
                     off = ((tile * 2 + kb) * 1024) + kc * 128 + r * 8
                     assert torch.equal(p[off:off + 8], wc[tile * 16 + r, kb * 64 + kc * 8: kb * 64 + kc * 8 + 8])
+
+
+def test_pack_slabs_layout():
+    w = torch.arange(32 * 128, device="cuda", dtype=torch.int32).reshape(32, 128).remainder(251).sub(125).to(torch.int8)
+    p = mq.pack_tiles(w, slab_major=True).cpu().view(-1)
+    wc = w.cpu()
+    # block (kb, tile) at ((kb * rows/16) + tile) * 1024, inside [8-col group][16 rows][8 bytes]
+    for tile in range(2):
+        for kb in range(2):
+            for kc in range(8):
+                for r in range(16):
+                    off = ((kb * 2 + tile) * 1024) + kc * 128 + r * 8
+                    assert torch.equal(p[off:off + 8], wc[tile * 16 + r, kb * 64 + kc * 8: kb * 64 + kc * 8 + 8])

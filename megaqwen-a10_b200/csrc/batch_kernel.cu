@@ -7,10 +7,10 @@
 // moves through plain global buffers):
 //   QKV   GEMM on the 5th-generation tensor cores (tcgen05.mma, accumulator in
 //         TMEM) -> qkv[b][4096] fp32
-//   ATTN  one warp per (sequence, KV head, 256-position split): QK-RMSNorm +
-//         RoPE at the sequence's own position, K/V write, flash-decode over
+//   ATTN  one equal range of (sequence, KV head, position) per warp: QK-RMSNorm
+//         + RoPE at the sequence's own position, K/V write, flash-decode over
 //         the cached positions (KV chunks bulk-copied into the warp's shared
-//         buffer)  -> split partials (m, l, acc)
+//         buffer) -> partials (m, l, acc)
 //   MERGE one warp per (sequence, q head): merges the splits -> O operand
 //   O     GEMM + residual -> act fp32, GU operand
 //   GU    gate and up GEMM, SiLU(gate)*up -> DOWN operand
@@ -737,15 +737,19 @@ __device__ void merge_item(const Smem* sm, const Params& P, int b, int qh) {
     const int c_len = P.positions[b] + 1;
     const int ns = nseg_of(sm->seqoff[b] + kvh * c_len, c_len, sm->segq);
     const float* base = P.part + ((size_t)b * NKVH + kvh) * MAX_SPLITS_B * PARTW;
-    float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * PARTW + 2 * HD + hh));
-    float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    // one online pass over the partials (loads do not depend on the running state)
+    float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
     for (int s = 0; s < ns; ++s) {
         const float* ps = base + (size_t)s * PARTW;
-        const float e = expf(__ldcg(ps + 2 * HD + hh) - M);
-        L = fmaf(__ldcg(ps + 2 * HD + 2 + hh), e, L);
+        const float ms = __ldcg(ps + 2 * HD + hh), ls = __ldcg(ps + 2 * HD + 2 + hh);
         const float4 a = __ldcg(reinterpret_cast<const float4*>(ps + hh * HD + 4 * lane));
-        o[0] = fmaf(a.x, e, o[0]); o[1] = fmaf(a.y, e, o[1]); o[2] = fmaf(a.z, e, o[2]); o[3] = fmaf(a.w, e, o[3]);
+        const float Mn = fmaxf(M, ms);
+        const float cprev = expf(M - Mn), cs = expf(ms - Mn);
+        L = L * cprev + ls * cs;
+        o[0] = o[0] * cprev + a.x * cs; o[1] = o[1] * cprev + a.y * cs;
+        o[2] = o[2] * cprev + a.z * cs; o[3] = o[3] * cprev + a.w * cs;
+        M = Mn;
     }
     const float inv = XS_ACT / L;
     uint32_t w[2];

@@ -70,7 +70,12 @@ constexpr int ACC_COLS = 256;            // fp32 accumulator columns (N <= 256)
 constexpr int TMEM_COLS = NMMA == 1 ? 256 : 512;   // one accumulator per MMA issuer
 constexpr int MAX_TILES_PASS = ACC_COLS / TROWS;
 constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension (sum-of-squares partials)
-constexpr int ACH = 16;                  // positions per KV chunk copy
+#ifndef MQB_ACH
+#define MQB_ACH 16
+#endif
+constexpr int ACH = MQB_ACH;             // positions per KV chunk copy (8 or 16)
+constexpr int NBUF = 32 / ACH;           // KV chunk buffers per warp (same 16 KB per warp)
+constexpr int LPP = 16 / ACH;            // lanes per (head, position) for the scores
 constexpr int MAX_SPLITS_B = 130;        // partials per (sequence, KV head): 32768 / 256 + 2
 constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
 
@@ -124,7 +129,7 @@ struct Params {
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
 struct AttnSmem {
-    alignas(16) uint8_t kv[NW][2][2 * ACH * HD * 2];   // per warp: two chunks of 16 positions (K then V)
+    alignas(16) uint8_t kv[NW][NBUF][2 * ACH * HD * 2];   // per warp: NBUF chunks of ACH positions (K then V)
     alignas(16) float q[NW][2][HD];
 };
 struct Smem {
@@ -135,7 +140,7 @@ struct Smem {
     uint64_t full[NR];       // slab copies landed
     uint64_t mdone[NR];      // MMAs reading the slot completed (tcgen05.commit)
     uint64_t deq[NR];        // slot's weights dequantised (one arrival per dequantising warp)
-    uint64_t abar[NW][2];    // per-warp KV chunk copies (two buffers)
+    uint64_t abar[NW][NBUF]; // per-warp KV chunk copies
     unsigned long long tokbest[BMAX];
     float rstd[BMAX];        // per-sequence 1/rms of the GEMM input being consumed
     int seqoff[BMAX + 1];    // attention work split: flattened start of each sequence
@@ -560,7 +565,8 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
     c.mma_par = 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); mbar_init(&sm->deq[i], NDQ); }
-        for (int i = 0; i < NW; ++i) { mbar_init(&sm->abar[i][0], 1); mbar_init(&sm->abar[i][1], 1); }
+        for (int i = 0; i < NW; ++i)
+            for (int j = 0; j < NBUF; ++j) mbar_init(&sm->abar[i][j], 1);
         sm->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -635,9 +641,10 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         }
     }
     __syncwarp();
-    // lane = (head hq of the pair, position pl of a 16-position chunk) for the scores;
-    // lane owns dims [4 lane, 4 lane + 4) of both heads for the output.
-    const int hq = lane >> 4, pl = lane & 15;
+    // Scores: lane = (head hq of the pair, position pl of the chunk, part hf of
+    // the 128 dims when LPP = 2 lanes share a position); output: lane owns dims
+    // [4 lane, 4 lane + 4) of both heads.
+    const int hq = lane >> 4, pl = (lane & 15) / LPP, hf = lane & (LPP - 1);
     float m = -INFINITY, lsum = 0.f;          // running max / sum of this lane's head
     float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     const float scale = P.attn_scale;
@@ -649,9 +656,11 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         if (pl < n) {
             const uint16_t* kr = kb + pl * HD;
             float x0 = 0.f, x1 = 0.f;
+            constexpr int D4 = HD / 4 / LPP;   // 4-dim groups per lane
 #pragma unroll 8
-            for (int i = 0; i < HD / 4; ++i) {
-                const int d4 = (pl + i) & (HD / 4 - 1);   // rotated: the 16 rows hit distinct banks
+            for (int i = 0; i < D4; ++i) {
+                // rotated so that the lanes' rows (and halves) hit distinct banks
+                const int d4 = hf * D4 + ((i + pl + (D4 / 2) * hf) & (D4 - 1));
                 const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * d4);
                 const float4 qa = qv[d4];
                 x0 = fmaf(qa.x, bf16_bits_to_f32(kw.x & 0xffffu), x0);
@@ -659,24 +668,26 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
                 x0 = fmaf(qa.z, bf16_bits_to_f32(kw.y & 0xffffu), x0);
                 x1 = fmaf(qa.w, bf16_bits_to_f32(kw.y >> 16), x1);
             }
-            sc = (x0 + x1) * scale;
+            sc = x0 + x1;
         }
+        if (LPP == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+        sc = pl < n ? sc * scale : -INFINITY;
         float mx = sc;
 #pragma unroll
-        for (int o = 8; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int o = 8; o >= LPP; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         const float nm = fmaxf(m, mx);
         const float cf = expf(m - nm);
         const float e = pl < n ? expf(sc - nm) : 0.f;
         float es = e;
 #pragma unroll
-        for (int o = 8; o; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
+        for (int o = 8; o >= LPP; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
         lsum = lsum * cf + es;
         m = nm;
         const float c0 = __shfl_sync(0xffffffffu, cf, 0), c1 = __shfl_sync(0xffffffffu, cf, 16);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
         for (int p = 0; p < n; ++p) {
-            const float ep0 = __shfl_sync(0xffffffffu, e, p), ep1 = __shfl_sync(0xffffffffu, e, 16 + p);
+            const float ep0 = __shfl_sync(0xffffffffu, e, p * LPP), ep1 = __shfl_sync(0xffffffffu, e, 16 + p * LPP);
             const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * lane);
             const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
             const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
@@ -684,35 +695,36 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
             a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
         }
     };
-    // cached positions [p0, p1) in 16-position chunks, two in flight per warp
+    // cached positions [p0, p1) in ACH-position chunks, NBUF in flight per warp
     const size_t head = (((size_t)b * P.L + l) * NKVH + kvh) * (size_t)P.max_seq * HD;
     const int nch = (p1 - p0 + ACH - 1) / ACH;
     auto issue = [&](int ci) {   // lane 0
         const int p = p0 + ACH * ci, n = min(ACH, p1 - p);
-        uint8_t* buf = sm->a.kv[warp][ci & 1];
+        const int bi = ci % NBUF;
+        uint8_t* buf = sm->a.kv[warp][bi];
         fence_proxy_async();
-        mbar_arrive_expect_tx(&sm->abar[warp][ci & 1], 2u * n * HD * 2);
-        bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][ci & 1]);
-        bulk_g2s(buf + ACH * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][ci & 1]);
+        mbar_arrive_expect_tx(&sm->abar[warp][bi], 2u * n * HD * 2);
+        bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][bi]);
+        bulk_g2s(buf + ACH * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][bi]);
     };
     __syncwarp();
-    for (int ci = 0; ci < min(2, nch); ++ci) {
+    for (int ci = 0; ci < min(NBUF, nch); ++ci) {
         if (lane == 0) issue(ci);
-        apend |= 1u << (ci & 1);
+        apend |= 1u << ci;
     }
     for (int ci = 0; ci < nch; ++ci) {
-        const int bs = ci & 1;
+        const int bs = ci % NBUF;
         if (!mbar_wait_b(c, &sm->abar[warp][bs], (ause >> bs) & 1u, 300)) return;
         apend &= ~(1u << bs);
         ause ^= 1u << bs;
         chunk(sm->a.kv[warp][bs], min(ACH, p1 - p0 - ACH * ci));
         __syncwarp();
-        if (ci + 2 < nch) {
-            if (lane == 0) issue(ci + 2);
+        if (ci + NBUF < nch) {
+            if (lane == 0) issue(ci + NBUF);
             apend |= 1u << bs;
         }
     }
-    if (owner) {  // the current position from registers (both buffers are free now)
+    if (owner) {  // the current position from registers (all buffers are free now)
         uint16_t* kw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0]);
         uint16_t* vw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0] + ACH * HD * 2);
 #pragma unroll
@@ -1007,7 +1019,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         }
     }
     if (lane == 0)
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < NBUF; ++i)
             if (apend & (1u << i)) mbar_drain(&sm->abar[warp][i], (ause >> i) & 1u, P.budget_ns);
     drain_and_free(c);
     __syncthreads();

@@ -216,6 +216,11 @@ typedef struct MQBatchArgs {
     int num_layers;
     int max_seq_len;
     float attn_scale;
+    int prefill;                         /* 0: independent sequences.  1: chunked prefill -- the rows are
+                                            consecutive tokens of ONE sequence at consecutive positions,
+                                            all sharing the cache of row 0 ([num_layers][8][max_seq][128]);
+                                            every row's K/V is written before attention, which reads
+                                            positions [0, position] from the cache; num_steps must be 1 */
 } MQBatchArgs;
 
 int mq_batch_workspace_bytes(int batch, size_t* bytes);

@@ -123,6 +123,7 @@ struct Params {
     unsigned long long budget_ns;
     int B, L, max_seq;
     float attn_scale;
+    int prefill;                // rows = consecutive tokens of ONE sequence sharing row 0's KV cache
 };
 
 // ---------------------------------------------------------------------------
@@ -587,6 +588,42 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
 // needs no bookkeeping.
 __device__ __forceinline__ int nseg_of(int F, int c_len, int Q) { return (F + c_len - 1) / Q - F / Q + 1; }
 
+// QK-RMSNorm + split-half RoPE of one 128-dim head (lane holds dims lane + 32j; partners j, j + 2).
+__device__ __forceinline__ void norm_rope(const float* raw, const __nv_bfloat16* nw, const __nv_bfloat16* cosr,
+                                          const __nv_bfloat16* sinr, int lane, float out[4]) {
+    float v[4], ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { v[j] = __ldcg(raw + lane + 32 * j); ss += v[j] * v[j]; }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)HD + RMS_EPS);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * __bfloat162float(nw[lane + 32 * j]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int i = lane + 32 * j;
+        out[j] = v[j] * __bfloat162float(cosr[i]) - v[j + 2] * __bfloat162float(sinr[i]);
+        out[j + 2] = v[j] * __bfloat162float(sinr[i + 64]) + v[j + 2] * __bfloat162float(cosr[i + 64]);
+    }
+}
+
+// Prefill: K (normed, rotated) and V of row b's token for KV head kvh into the
+// shared cache at the row's position (one warp).
+__device__ void kv_write_item(const Params& P, int l, int b, int kvh) {
+    const int lane = threadIdx.x & 31;
+    const int pos = P.positions[b];
+    const float* qkv = P.qkv + (size_t)b * QKV_ROWS;
+    float o[4];
+    norm_rope(qkv + QSZ + kvh * HD, (const __nv_bfloat16*)P.layers[l].k_norm_weight, P.cos_t + (size_t)pos * HD,
+              P.sin_t + (size_t)pos * HD, lane, o);
+    const size_t off = (((size_t)l * NKVH + kvh) * (size_t)P.max_seq + pos) * HD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = lane + 32 * j;
+        reinterpret_cast<uint16_t*>(P.kc)[off + i] = (uint16_t)f32_to_bf16_bits(o[j]);
+        reinterpret_cast<uint16_t*>(P.vc)[off + i] = (uint16_t)f32_to_bf16_bits(__ldcg(qkv + QSZ + KVSZ + kvh * HD + i));
+    }
+}
+
 // Positions [pa, pb) of (b, kvh) -> partial s.  The piece with pb = cache_len
 // owns the current position: it writes K/V there and takes it from registers.
 __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa, int pb, int s, uint32_t& ause,
@@ -596,41 +633,26 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
     const int pos = P.positions[b];
     const int c_len = pos + 1;
     const int p0 = pa;
-    const bool owner = pb == c_len;
+    const bool owner = pb == c_len && !P.prefill; // prefill: this step's K/V are in the cache already
     const int p1 = owner ? pos : pb;              // cached positions [p0, p1)
+    const int cb = P.prefill ? 0 : b;             // cache row
     const LayerWeights& w = P.layers[l];
     const float* qkv = P.qkv + (size_t)b * QKV_ROWS;
     const __nv_bfloat16* cosr = P.cos_t + (size_t)pos * HD;
     const __nv_bfloat16* sinr = P.sin_t + (size_t)pos * HD;
     float* q = sm->a.q[warp][0];
-    // QK-RMSNorm + split-half RoPE (lane holds dims lane + 32j; partners j, j + 2)
-    auto norm_rope = [&](const float* raw, const __nv_bfloat16* nw, float out[4]) {
-        float v[4], ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { v[j] = __ldcg(raw + lane + 32 * j); ss += v[j] * v[j]; }
-        ss = warp_sum(ss);
-        const float r = rsqrtf(ss / (float)HD + RMS_EPS);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = v[j] * r * __bfloat162float(nw[lane + 32 * j]);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int i = lane + 32 * j;
-            out[j] = v[j] * __bfloat162float(cosr[i]) - v[j + 2] * __bfloat162float(sinr[i]);
-            out[j + 2] = v[j] * __bfloat162float(sinr[i + 64]) + v[j + 2] * __bfloat162float(cosr[i + 64]);
-        }
-    };
 #pragma unroll
     for (int hq = 0; hq < 2; ++hq) {
         float o[4];
-        norm_rope(qkv + (2 * kvh + hq) * HD, (const __nv_bfloat16*)w.q_norm_weight, o);
+        norm_rope(qkv + (2 * kvh + hq) * HD, (const __nv_bfloat16*)w.q_norm_weight, cosr, sinr, lane, o);
 #pragma unroll
         for (int j = 0; j < 4; ++j) q[hq * HD + lane + 32 * j] = o[j];
     }
     uint16_t kcur[4], vcur[4];
     if (owner) {
         float o[4];
-        norm_rope(qkv + QSZ + kvh * HD, (const __nv_bfloat16*)w.k_norm_weight, o);
-        const size_t off = ((((size_t)b * P.L + l) * NKVH + kvh) * (size_t)P.max_seq + pos) * HD;
+        norm_rope(qkv + QSZ + kvh * HD, (const __nv_bfloat16*)w.k_norm_weight, cosr, sinr, lane, o);
+        const size_t off = ((((size_t)cb * P.L + l) * NKVH + kvh) * (size_t)P.max_seq + pos) * HD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int i = lane + 32 * j;
@@ -696,7 +718,7 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         }
     };
     // cached positions [p0, p1) in ACH-position chunks, NBUF in flight per warp
-    const size_t head = (((size_t)b * P.L + l) * NKVH + kvh) * (size_t)P.max_seq * HD;
+    const size_t head = (((size_t)cb * P.L + l) * NKVH + kvh) * (size_t)P.max_seq * HD;
     const int nch = (p1 - p0 + ACH - 1) / ACH;
     auto issue = [&](int ci) {   // lane 0
         const int p = p0 + ACH * ci, n = min(ACH, p1 - p);
@@ -861,6 +883,10 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         }
         stamp(P, l * 8 + 1);
         if (!grid_barrier(c, 1)) { ok = false; break; }
+        if (P.prefill) {   // every row's K/V in the cache before any attention reads it
+            for (int it = cta * NW + warp; it < B * NKVH; it += nb * NW) kv_write_item(P, l, it / NKVH, it % NKVH);
+            if (!grid_barrier(c, 8)) { ok = false; break; }
+        }
         // ---- attention ----
         {
             const int Q = sm->segq, T = sm->seqoff[B];
@@ -1290,6 +1316,8 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     P.L = a->num_layers;
     P.max_seq = a->max_seq_len;
     P.attn_scale = a->attn_scale;
+    P.prefill = a->prefill;
+    if (P.prefill && num_steps != 1) return MQ_ERR_ARG;
     void* args[] = {&P};
     for (int j = 0; j < num_steps; ++j) {
         e = cudaLaunchCooperativeKernel((const void*)batch_kernel, dim3(g_sms[dev]), dim3(NT), args, sizeof(Smem), stream);

@@ -28,6 +28,7 @@ class MQBatchArgs(ctypes.Structure):
         ("logits", ctypes.c_void_p), ("trace", ctypes.c_void_p), ("wait_budget_ns", ctypes.c_ulonglong),
         ("batch", ctypes.c_int),
         ("num_layers", ctypes.c_int), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
+        ("prefill", ctypes.c_int),
     ]
 
 
@@ -73,6 +74,90 @@ def batch_matmul(w_tiles, scale, x):
     return y
 
 
+def packed_weights(dec):
+    """(device LayerWeights table of the tile-packed projections, slab-packed LM
+    head) of an A10Int8MegakernelDecoder, built once and kept on the decoder."""
+    pk = getattr(dec, "_packed_", None)
+    if pk is None:
+        keep = []
+        arr = (_lib.LayerWeights * dec.num_layers_)()
+        flat = dec.layer_weights_flat_
+        for i in range(dec.num_layers_):
+            for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
+                t = flat[i * 11 + j]
+                if t.dim() == 2:
+                    t = pack_tiles(t)
+                    keep.append(t)
+                setattr(arr[i], fname, t.data_ptr())
+        table = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dec.device)
+        lm = pack_tiles(dec.lm_head_weight_, slab_major=True)
+        pk = dec._packed_ = (table, lm, keep)
+    return pk[0], pk[1]
+
+
+def _launch(dec, table, lm, kc, vc, tokens, positions, ws, batch, max_seq, num_steps, logits, trace, prefill):
+    a = MQBatchArgs(dec.embed_weight_.data_ptr(), table.data_ptr(), dec.d_layer_scales_.data_ptr(),
+                    dec.final_norm_weight_.data_ptr(), lm.data_ptr(), dec.lm_head_scale_.data_ptr(),
+                    dec.cos_table_.data_ptr(), dec.sin_table_.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                    tokens.data_ptr(), positions.data_ptr(), ws.data_ptr(), ws.numel(),
+                    logits.data_ptr() if logits is not None else None,
+                    trace.data_ptr() if trace is not None else None, 0, batch, dec.num_layers_, max_seq,
+                    dec.attn_scale_, int(prefill))
+    with torch.cuda.device(dec.device):
+        stream = torch.cuda.current_stream(dec.device).cuda_stream
+        rc = _lib.load().mq_batch_decode(ctypes.byref(a), int(num_steps), ctypes.c_void_p(stream))
+    _lib.check(rc, "mq_batch_decode")
+
+
+def _status(ws):
+    code, info = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().mq_batch_status(ctypes.c_void_p(ws.data_ptr()), ctypes.byref(code), ctypes.byref(info)),
+               "mq_batch_status")
+    return code.value, info.value
+
+
+class Prefiller:
+    """Chunked prefill of one sequence into an A10Int8MegakernelDecoder's own KV
+    cache: up to 64 prompt tokens per launch go through the batched tensor-core
+    kernel as rows of one sequence (MQBatchArgs.prefill = 1).  Replaces feeding
+    the prompt one decode step per token (a10_decode.py:366-369)."""
+    CHUNK = 64
+
+    def __init__(self, dec):
+        if dec.max_seq_len_ > 32768:
+            raise ValueError("prefill needs max_seq_len <= 32768")
+        self.dec = dec
+        self.table, self.lm = packed_weights(dec)
+        dev = dec.device
+        self.tokens = torch.zeros(self.CHUNK, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(self.CHUNK, dtype=torch.int32, device=dev)
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(_lib.load().mq_batch_workspace_bytes(self.CHUNK, ctypes.byref(nbytes)), "mq_batch_workspace_bytes")
+        self.workspace = torch.zeros(nbytes.value, dtype=torch.uint8, device=dev)
+
+    def run(self, ids, start, logits=None):
+        """Tokens ids at positions start .. start + len(ids) - 1; returns the device
+        int32 vector of the last chunk's argmax outputs (its last entry is the
+        greedy next token).  logits (optional): fp32 [len(last chunk), vocab]."""
+        d = self.dec
+        out = None
+        for c0 in range(0, len(ids), self.CHUNK):
+            chunk = ids[c0:c0 + self.CHUNK]
+            n = len(chunk)
+            self.tokens[:n].copy_(torch.as_tensor(chunk, dtype=torch.int32))
+            self.positions[:n].copy_(torch.arange(start + c0, start + c0 + n, dtype=torch.int32))
+            last = c0 + self.CHUNK >= len(ids)
+            _launch(d, self.table, self.lm, d.k_cache_, d.v_cache_, self.tokens, self.positions, self.workspace, n,
+                    d.max_seq_len_, 1, logits if last else None, None, True)
+            out = self.tokens[:n]
+        return out
+
+    def check_device(self):
+        code, info = _status(self.workspace)
+        if code:
+            raise _lib.MQError(f"prefill: device error {code} ({_lib.MQ_DEV_ERRORS.get(code, '?')}, at {info})")
+
+
 class BatchedDecoder:
     MAX_BATCH = 64
 
@@ -85,19 +170,7 @@ class BatchedDecoder:
             raise ValueError("max_seq_len out of range")
         self.w = weights
         self.device = weights.device
-        # tile-packed INT8 matrices (norm weights and q/k norms unchanged)
-        self._tiles = []
-        arr = (_lib.LayerWeights * weights.num_layers_)()
-        flat = weights.layer_weights_flat_
-        for i in range(weights.num_layers_):
-            for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
-                t = flat[i * 11 + j]
-                if t.dim() == 2:
-                    t = pack_tiles(t)
-                    self._tiles.append(t)
-                setattr(arr[i], fname, t.data_ptr())
-        self.d_layer_tiles_ = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(self.device)
-        self.lm_head_tiles_ = pack_tiles(weights.lm_head_weight_, slab_major=True)
+        self.d_layer_tiles_, self.lm_head_tiles_ = packed_weights(weights)
         self.B, self.L, self.max_seq_len = batch, weights.num_layers_, max_seq_len
         shape = (batch, self.L, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
         self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
@@ -126,26 +199,12 @@ class BatchedDecoder:
         no host sync).  Returns the device token vector (the last step's outputs)."""
         if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (self.B, VOCAB_SIZE)):
             raise ValueError("logits must be fp32 [batch, vocab]")
-        w = self.w
-        a = MQBatchArgs(w.embed_weight_.data_ptr(), self.d_layer_tiles_.data_ptr(), w.d_layer_scales_.data_ptr(),
-                        w.final_norm_weight_.data_ptr(), self.lm_head_tiles_.data_ptr(), w.lm_head_scale_.data_ptr(),
-                        w.cos_table_.data_ptr(), w.sin_table_.data_ptr(), self.k_cache.data_ptr(),
-                        self.v_cache.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
-                        self.workspace.data_ptr(), self.workspace.numel(),
-                        logits.data_ptr() if logits is not None else None,
-                        trace.data_ptr() if trace is not None else None, 0, self.B, self.L,
-                        self.max_seq_len, w.attn_scale_)
-        with torch.cuda.device(self.device):
-            stream = torch.cuda.current_stream(self.device).cuda_stream
-            rc = _lib.load().mq_batch_decode(ctypes.byref(a), int(num_steps), ctypes.c_void_p(stream))
-        _lib.check(rc, "mq_batch_decode")
+        _launch(self.w, self.d_layer_tiles_, self.lm_head_tiles_, self.k_cache, self.v_cache, self.tokens,
+                self.positions, self.workspace, self.B, self.max_seq_len, num_steps, logits, trace, False)
         return self.tokens
 
     def status(self):
-        code, info = ctypes.c_int(0), ctypes.c_int(0)
-        _lib.check(_lib.load().mq_batch_status(ctypes.c_void_p(self.workspace.data_ptr()), ctypes.byref(code),
-                                               ctypes.byref(info)), "mq_batch_status")
-        return code.value, info.value
+        return _status(self.workspace)
 
     def check_device(self):
         code, info = self.status()

@@ -241,6 +241,27 @@ class A10Int8MegakernelDecoder(_MegakernelDecoderBase):
                 setattr(arr[i], fname, layer_scales_all[i * 7 + j].data_ptr())
         self.d_layer_scales_ = self._to_device_bytes(arr)
 
+    def prefill(self, token_ids, logits=None):
+        """Feeds prompt tokens at positions position() .. position() + n - 1 in
+        chunks of up to 64 through the batched tensor-core kernel (one launch per
+        chunk, the KV cache filled as by n decode steps) and returns the greedy
+        next token (int).  logits (optional): fp32 [n of the last chunk, vocab]."""
+        ids = [int(t) for t in token_ids]
+        if not ids:
+            raise ValueError("empty prompt")
+        if any(t < 0 or t >= VOCAB_SIZE for t in ids):
+            raise ValueError("token out of range")
+        if self.position_ + len(ids) > self.max_seq_len_:
+            raise ValueError("prompt exceeds max_seq_len")
+        if getattr(self, "_prefiller", None) is None:
+            from .batch import Prefiller
+            self._prefiller = Prefiller(self)
+        out = self._prefiller.run(ids, self.position_, logits)
+        self.position_ += len(ids)
+        nxt = int(out[-1].item())
+        self._prefiller.check_device()
+        return nxt
+
     def _scale_ptrs(self):
         return _ptr(self.lm_head_scale_), _ptr(self.d_layer_scales_)
 
@@ -329,16 +350,20 @@ class A10Decoder:
 
     def generate(self, prompt, max_new_tokens=128, eos_token_id=None):
         """Greedy generation.  `prompt` is a list of token ids, or a string when a
-        tokenizer was given.  The prompt is fed one token per step, as in the
-        reference (a10_decode.py:366-369).  Returns the generated id list (or
+        tokenizer was given.  INT8: the prompt goes through the chunked prefill
+        (64 tokens per launch); BF16: one token per step, as in the reference
+        (a10_decode.py:366-369).  Returns the generated id list (or
         text with a tokenizer)."""
         ids = self.tokenizer.encode(prompt) if isinstance(prompt, str) else list(prompt)
         if not ids:
             raise ValueError("empty prompt")
         self.reset()
-        nxt = None
-        for t in ids:
-            nxt = self.decoder.decode_step(t)
+        if hasattr(self.decoder, "prefill"):   # INT8: chunked prefill on the tensor cores
+            nxt = self.decoder.prefill(ids)
+        else:
+            nxt = None
+            for t in ids:
+                nxt = self.decoder.decode_step(t)
         out = list(ids)
         for _ in range(max_new_tokens):
             out.append(nxt)

@@ -175,6 +175,43 @@ def run_long_context(args):
                       "config": {"workload": "config3", "context": ctx, "kv": "seeded N(0,1) bf16"}}), flush=True)
 
 
+def run_prefill(args):
+    """Chunked prefill (64 tokens per launch on the tensor-core path) of an
+    args.prefill-token prompt vs the same prompt fed one decode step per token."""
+    n, L = args.prefill, args.layers
+    dec = build_decoder(L, n + 8)
+    ids = torch.randint(0, 151936, (n,), generator=torch.Generator().manual_seed(5)).tolist()
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(max(args.warmup, 3)):
+        dec.reset()
+        dec.prefill(ids)
+    times = []
+    for _ in range(max(args.steps, 1)):
+        dec.reset()
+        torch.cuda.synchronize()
+        a.record(stream)
+        dec.prefill(ids)
+        b.record(stream)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    dec.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for t in ids:
+        dec.decode_step(t)
+    step_ms = (time.perf_counter() - t0) * 1000.0
+    line = {"metric": "prefill tok/s (chunked, 64 tokens per launch)", "value": round(n / (ms / 1000.0), 1),
+            "unit": "tok/s", "n_gpus": 1, "steps": len(times), "warmup": max(args.warmup, 3), "ms": round(ms, 3),
+            "higher_is_better": True, "dtype": "int8-weights/fp16-activations/fp32-accum", "data": "synthetic",
+            "config": {"workload": f"prefill of a {n}-token prompt, {L} layers", "prompt_tokens": n},
+            "stepwise": {"ms": round(step_ms, 3), "tok_s": round(n / (step_ms / 1000.0), 1),
+                         "api": "decode_step(int) per prompt token"},
+            "gpu_launches": (n + 63) // 64}
+    print(json.dumps(line), flush=True)
+
+
 def run_batched(args, rank, world, dist):
     """64 independent sequences per GPU, positions drawn
     uniformly from 128..2048 (seeded per rank), KV caches pre-filled with seeded
@@ -299,6 +336,9 @@ def main():
                     help="BASELINE config: 1 INT8 (default, the headline), 2 BF16 weights, 3 long context, "
                          "4 batched (64 sequences per GPU)")
     ap.add_argument("--context", type=int, default=4096, help="config 3: cached positions before the timed step")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="time the chunked prefill of a prompt of this many tokens (INT8, 28 layers) "
+                         "against feeding it one decode step per token")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -319,6 +359,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     torch.cuda.set_device(local)
     from megaqwen_b200 import _lib
+    if args.prefill:
+        run_prefill(args)
+        return
     if args.config == 3:
         run_long_context(args)
         return

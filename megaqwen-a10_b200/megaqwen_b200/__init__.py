@@ -10,7 +10,7 @@ from .rope import make_rope
 from .synth import make_synthetic_state
 from .decoder import A10Decoder, A10Int8MegakernelDecoder, A10MegakernelDecoder, layer_lists
 from .batch import BatchedDecoder, batch_matmul, pack_tiles
-from . import _lib
+from . import _lib, checkpoint
 from ._lib import MQError
 
 __all__ = ["CFG", "Qwen3Config", "quantize_per_channel", "quantize_state", "make_rope", "make_synthetic_state",

@@ -324,16 +324,24 @@ class A10Decoder:
     ``synth.make_synthetic_state`` or a real checkpoint's ``state_dict()``);
     ``quantized=True`` builds the INT8 decoder, else the BF16 one.
     ``generate`` takes token ids (and an optional tokenizer for text in/out).
+    ``quantized_state`` (INT8 only) is an already quantized state (quantize_state's
+    output, e.g. from checkpoint.load_quantized): startup quantization is skipped.
+    ``from_pretrained`` builds one from a checkpoint directory.
     """
 
     def __init__(self, state, quantized=True, max_seq_len=MAX_SEQ_LEN, num_layers=NUM_LAYERS, device="cuda",
-                 tokenizer=None):
+                 tokenizer=None, quantized_state=None):
         self.device = torch.device(device)
         self.max_seq_len = max_seq_len
         self.tokenizer = tokenizer
         cos, sin = make_rope(max_seq_len, HEAD_DIM, device=self.device, theta=CFG.rope_theta)
         if quantized:
-            q = quantize_state(state, num_layers=num_layers, device=self.device)
+            if quantized_state is not None:
+                q = {k: (v[0].to(self.device), v[1].to(self.device)) if isinstance(v, tuple) else v.to(self.device)
+                     for k, v in quantized_state.items()}
+            else:
+                q = quantize_state(state, num_layers=num_layers, device=self.device)
+            self.quantized_state = q
             layers, scales = layer_lists(q, num_layers, True)
             lm_q, lm_s = q["lm_head.weight"]
             self.decoder = A10Int8MegakernelDecoder(q["model.embed_tokens.weight"], layers, scales, lm_q, lm_s,
@@ -344,6 +352,33 @@ class A10Decoder:
             lm = st.get("lm_head.weight", st["model.embed_tokens.weight"])
             self.decoder = A10MegakernelDecoder(st["model.embed_tokens.weight"], layers, st["model.norm.weight"],
                                                 lm, cos, sin, num_layers, max_seq_len)
+
+    @classmethod
+    def from_pretrained(cls, path, quantized=True, max_seq_len=MAX_SEQ_LEN, num_layers=NUM_LAYERS, device="cuda",
+                        tokenizer=True, quantized_path=None):
+        """Decoder from an HF Qwen3 checkpoint directory (safetensors).  tokenizer=True
+        loads the directory's tokenizer with transformers (local files only) when
+        present.  quantized_path: a file written by checkpoint.save_quantized; used
+        instead of quantizing when it exists, written after quantizing when not."""
+        import os
+        from . import checkpoint as ck
+        tok = None
+        if tokenizer is True:
+            if os.path.exists(os.path.join(path, "tokenizer.json")) or os.path.exists(os.path.join(path, "tokenizer_config.json")):
+                from transformers import AutoTokenizer
+                tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+        elif tokenizer:
+            tok = tokenizer
+        if quantized and quantized_path and os.path.exists(quantized_path):
+            q, n = ck.load_quantized(quantized_path)
+            if n != num_layers:
+                raise ValueError(f"{quantized_path} holds {n} layers, not {num_layers}")
+            return cls(None, True, max_seq_len, num_layers, device, tok, quantized_state=q)
+        state = ck.load_state(path, num_layers=num_layers)
+        dec = cls(state, quantized, max_seq_len, num_layers, device, tok)
+        if quantized and quantized_path:
+            ck.save_quantized(dec.quantized_state, quantized_path, num_layers=num_layers)
+        return dec
 
     def reset(self):
         self.decoder.reset()

@@ -383,6 +383,26 @@ class A10Decoder:
     def reset(self):
         self.decoder.reset()
 
+    def stream(self, prompt, max_new_tokens=128, eos_token_id=None):
+        """Like generate, but yields each new token id as soon as it is decoded (the
+        decoded text piece instead when a tokenizer was given), for streaming chat
+        front ends (the reference's a10_chat.py prints tokens as they come)."""
+        ids = self.tokenizer.encode(prompt) if isinstance(prompt, str) else list(prompt)
+        if not ids:
+            raise ValueError("empty prompt")
+        self.reset()
+        nxt = self.decoder.prefill(ids) if hasattr(self.decoder, "prefill") else None
+        if nxt is None:
+            for t in ids:
+                nxt = self.decoder.decode_step(t)
+        for i in range(max_new_tokens):
+            yield self.tokenizer.decode([nxt]) if self.tokenizer is not None else nxt
+            if eos_token_id is not None and nxt == eos_token_id:
+                return
+            if i + 1 == max_new_tokens or self.decoder.position() >= self.max_seq_len:
+                return
+            nxt = self.decoder.decode_step(nxt)
+
     def generate(self, prompt, max_new_tokens=128, eos_token_id=None):
         """Greedy generation.  `prompt` is a list of token ids, or a string when a
         tokenizer was given.  INT8: the prompt goes through the chunked prefill

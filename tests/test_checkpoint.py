@@ -83,3 +83,12 @@ def test_from_pretrained_decodes_like_in_memory(tmp_path):
     want = ref.generate(prompt, max_new_tokens=6)
     assert a.generate(prompt, max_new_tokens=6) == want
     assert b.generate(prompt, max_new_tokens=6) == want
+
+
+@pytest.mark.gpu
+def test_stream_yields_generate_tokens():
+    st = mq.make_synthetic_state(seed=5, num_layers=2)
+    d = mq.A10Decoder(st, quantized=True, max_seq_len=64, num_layers=2)
+    prompt = [3, 1, 4, 1, 5]
+    full = d.generate(prompt, max_new_tokens=7)
+    assert list(d.stream(prompt, max_new_tokens=7)) == full[len(prompt):]

@@ -221,6 +221,14 @@ typedef struct MQBatchArgs {
                                             all sharing the cache of row 0 ([num_layers][8][max_seq][128]);
                                             every row's K/V is written before attention, which reads
                                             positions [0, position] from the cache; num_steps must be 1 */
+    int vocab_shards, vocab_shard;       /* vocab-sharded LM head (G ranks decoding the same sequences):
+                                            this call scores only shard vocab_shard of vocab_shards
+                                            (contiguous 16-row tiles) and writes keys_out instead of tokens;
+                                            0 / 0: whole vocabulary */
+    long long* keys_out;                 /* [batch] packed argmax keys ((order(logit) << 32 | ~row) with the
+                                            sign bit flipped): the max over the shards (an int64 max
+                                            all-reduce) is the global argmax, lowest row on ties; the
+                                            token is ~key & 0xffffffff.  Requires num_steps == 1 */
 } MQBatchArgs;
 
 int mq_batch_workspace_bytes(int batch, size_t* bytes);

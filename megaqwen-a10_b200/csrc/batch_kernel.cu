@@ -124,6 +124,8 @@ struct Params {
     int B, L, max_seq;
     float attn_scale;
     int prefill;                // rows = consecutive tokens of ONE sequence sharing row 0's KV cache
+    int lm_tile0, lm_tiles;     // LM-head vocab shard: 16-row tiles [lm_tile0, lm_tile0 + lm_tiles)
+    long long* keys_out;        // vocab-sharded mode: per-sequence packed argmax keys (sign-flipped) instead of tokens
 };
 
 // ---------------------------------------------------------------------------
@@ -1009,7 +1011,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
     if (ok) {
         compute_rstd(sm, P.ss_a, B);
         const int NTL = VOCAB / TROWS;
-        const int T0 = split_lo(NTL, nb, cta), T1 = split_lo(NTL, nb, cta + 1);
+        const int T0 = P.lm_tile0 + split_lo(P.lm_tiles, nb, cta), T1 = P.lm_tile0 + split_lo(P.lm_tiles, nb, cta + 1);
         ok = tc_rows(c, P.xa_qkv, HIDDEN, T0, T1, [&](int g) { return P.lm_w + (size_t)g * TROWS * HIDDEN; },
                      [&](const float* E, int ldE, int g0, int nt) {
                          for (int i = threadIdx.x; i < B * nt; i += NT) {
@@ -1039,7 +1041,10 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         const bool err = ld_relaxed32(&P.ctl[2]) != 0;
         for (int t = threadIdx.x; t < B; t += NT) {
             const unsigned long long k = __ldcg(P.best + t);
-            P.tokens_out[t] = (err || k == 0ull) ? -1 : (int)(~(uint32_t)k);
+            if (P.keys_out)   // (logit order << 32 | ~row) with the sign bit flipped: a signed max-reduction keeps the order
+                P.keys_out[t] = err ? (long long)0x8000000000000000ull : (long long)(k ^ 0x8000000000000000ull);
+            else
+                P.tokens_out[t] = (err || k == 0ull) ? -1 : (int)(~(uint32_t)k);
             P.best[t] = 0ull;
             if (!err) P.positions[t] += 1;
         }
@@ -1317,6 +1322,16 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     P.max_seq = a->max_seq_len;
     P.attn_scale = a->attn_scale;
     P.prefill = a->prefill;
+    P.lm_tile0 = 0;
+    P.lm_tiles = VOCAB / TROWS;
+    P.keys_out = a->keys_out;
+    if (a->vocab_shards > 1 || a->keys_out) {
+        if (a->vocab_shards < 1 || a->vocab_shard < 0 || a->vocab_shard >= a->vocab_shards || !a->keys_out ||
+            num_steps != 1 || a->prefill)
+            return MQ_ERR_ARG;
+        P.lm_tile0 = split_lo(VOCAB / TROWS, a->vocab_shards, a->vocab_shard);
+        P.lm_tiles = split_lo(VOCAB / TROWS, a->vocab_shards, a->vocab_shard + 1) - P.lm_tile0;
+    }
     if (P.prefill && num_steps != 1) return MQ_ERR_ARG;
     void* args[] = {&P};
     for (int j = 0; j < num_steps; ++j) {

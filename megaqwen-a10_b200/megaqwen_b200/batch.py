@@ -28,7 +28,8 @@ class MQBatchArgs(ctypes.Structure):
         ("logits", ctypes.c_void_p), ("trace", ctypes.c_void_p), ("wait_budget_ns", ctypes.c_ulonglong),
         ("batch", ctypes.c_int),
         ("num_layers", ctypes.c_int), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
-        ("prefill", ctypes.c_int),
+        ("prefill", ctypes.c_int), ("vocab_shards", ctypes.c_int), ("vocab_shard", ctypes.c_int),
+        ("keys_out", ctypes.c_void_p),
     ]
 
 
@@ -95,14 +96,42 @@ def packed_weights(dec):
     return pk[0], pk[1]
 
 
-def _launch(dec, table, lm, kc, vc, tokens, positions, ws, batch, max_seq, num_steps, logits, trace, prefill):
+_SIGN = -(2 ** 63)
+
+
+def pack_keys(logits, row0=0):
+    """Host statement of the kernel's argmax key for fp32 logits [B, n] of vocab rows
+    row0 .. row0 + n - 1: (order(logit) << 32 | ~row) with the sign bit flipped, as
+    int64 [B] (the max over the rows).  Used to test the shard reduction."""
+    u = logits.float().contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    order = torch.where(u >= 2 ** 31, (~u) & 0xFFFFFFFF, u | 2 ** 31)
+    rows = torch.arange(row0, row0 + logits.shape[1], dtype=torch.int64)
+    k = (order << 32) | ((~rows) & 0xFFFFFFFF)
+    return (k ^ _SIGN).max(dim=1).values
+
+
+def reduce_shard_keys(keys, dist, group=None):
+    """Global argmax keys from every rank's vocab-shard keys (int64 max all-reduce, in place)."""
+    if dist is not None:
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+    return keys
+
+
+def keys_to_tokens(keys):
+    """Token ids (int32) from packed keys: the low 32 bits hold ~row."""
+    return ((~(keys ^ _SIGN)) & 0xFFFFFFFF).to(torch.int32)
+
+
+def _launch(dec, table, lm, kc, vc, tokens, positions, ws, batch, max_seq, num_steps, logits, trace, prefill,
+            shards=0, shard=0, keys=None):
     a = MQBatchArgs(dec.embed_weight_.data_ptr(), table.data_ptr(), dec.d_layer_scales_.data_ptr(),
                     dec.final_norm_weight_.data_ptr(), lm.data_ptr(), dec.lm_head_scale_.data_ptr(),
                     dec.cos_table_.data_ptr(), dec.sin_table_.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                     tokens.data_ptr(), positions.data_ptr(), ws.data_ptr(), ws.numel(),
                     logits.data_ptr() if logits is not None else None,
                     trace.data_ptr() if trace is not None else None, 0, batch, dec.num_layers_, max_seq,
-                    dec.attn_scale_, int(prefill))
+                    dec.attn_scale_, int(prefill), int(shards), int(shard),
+                    keys.data_ptr() if keys is not None else None)
     with torch.cuda.device(dec.device):
         stream = torch.cuda.current_stream(dec.device).cuda_stream
         rc = _lib.load().mq_batch_decode(ctypes.byref(a), int(num_steps), ctypes.c_void_p(stream))
@@ -161,15 +190,20 @@ class Prefiller:
 class BatchedDecoder:
     MAX_BATCH = 64
 
-    def __init__(self, weights, batch, max_seq_len):
+    def __init__(self, weights, batch, max_seq_len, vocab_shard=None):
         """weights: an A10Int8MegakernelDecoder (its INT8 matrices are tile-packed here);
-        max_seq_len <= 32768 and <= the rows of its RoPE tables."""
+        max_seq_len <= 32768 and <= the rows of its RoPE tables.
+        vocab_shard: (rank, world, dist, group) to split the LM head over `world`
+        ranks that decode the SAME sequences (same tokens and caches on every
+        rank): each scores 1/world of the vocabulary and one int64 max all-reduce
+        per step picks the global argmax (lowest index on ties)."""
         if not 1 <= batch <= self.MAX_BATCH:
             raise ValueError(f"batch must be in [1, {self.MAX_BATCH}]")
         if not 1 <= max_seq_len <= min(32768, weights.cos_table_.shape[0]):
             raise ValueError("max_seq_len out of range")
         self.w = weights
         self.device = weights.device
+        self.vocab_shard = vocab_shard
         self.d_layer_tiles_, self.lm_head_tiles_ = packed_weights(weights)
         self.B, self.L, self.max_seq_len = batch, weights.num_layers_, max_seq_len
         shape = (batch, self.L, NUM_KV_HEADS, max_seq_len, HEAD_DIM)
@@ -180,6 +214,7 @@ class BatchedDecoder:
         nbytes = ctypes.c_size_t(0)
         _lib.check(_lib.load().mq_batch_workspace_bytes(batch, ctypes.byref(nbytes)), "mq_batch_workspace_bytes")
         self.workspace = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
+        self.keys = torch.zeros(batch, dtype=torch.int64, device=self.device)
 
     def set_state(self, tokens, positions):
         """Input token and position (cache_len = position + 1) of every sequence."""
@@ -199,8 +234,17 @@ class BatchedDecoder:
         no host sync).  Returns the device token vector (the last step's outputs)."""
         if logits is not None and (logits.dtype != torch.float32 or tuple(logits.shape) != (self.B, VOCAB_SIZE)):
             raise ValueError("logits must be fp32 [batch, vocab]")
-        _launch(self.w, self.d_layer_tiles_, self.lm_head_tiles_, self.k_cache, self.v_cache, self.tokens,
-                self.positions, self.workspace, self.B, self.max_seq_len, num_steps, logits, trace, False)
+        if self.vocab_shard is None:
+            _launch(self.w, self.d_layer_tiles_, self.lm_head_tiles_, self.k_cache, self.v_cache, self.tokens,
+                    self.positions, self.workspace, self.B, self.max_seq_len, num_steps, logits, trace, False)
+            return self.tokens
+        rank, world, dist, group = self.vocab_shard
+        for _ in range(num_steps):   # one launch + one all-reduce per step
+            _launch(self.w, self.d_layer_tiles_, self.lm_head_tiles_, self.k_cache, self.v_cache, self.tokens,
+                    self.positions, self.workspace, self.B, self.max_seq_len, 1, None, trace, False,
+                    shards=world, shard=rank, keys=self.keys)
+            reduce_shard_keys(self.keys, dist if world > 1 else None, group)
+            self.tokens.copy_(keys_to_tokens(self.keys))
         return self.tokens
 
     def status(self):

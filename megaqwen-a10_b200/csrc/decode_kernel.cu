@@ -822,18 +822,35 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
     if (j < j1) {
         const int h = j >> 7;
         const int base_item = G.g * G.S;
-        float M = -INFINITY;
-        for (int t = 0; t < G.S; ++t)
-            M = fmaxf(M, __uint_as_float(poll_word(c, &part[(base_item + t) * PART_WORDS + 2 * HD + h], tp, 11)));
-        float L = 0.f, o = 0.f;
-        for (int t = 0; t < G.S; ++t) {
-            const uint64_t* pp = &part[(base_item + t) * PART_WORDS];
-            const float mt = __uint_as_float(poll_word(c, pp + 2 * HD + h, tp, 12));
-            const float lt = __uint_as_float(poll_word(c, pp + 2 * HD + 2 + h, tp, 12));
-            const float at = __uint_as_float(poll_word(c, pp + j, tp, 12));
-            const float e = expf(mt - M);
-            L = fmaf(lt, e, L);
-            o = fmaf(at, e, o);
+        // Online merge over the splits, MG at a time: the 3 * MG tagged words of a
+        // group are loaded together (one round trip), re-read only while a tag is missing.
+        constexpr int MG = 3;
+        float M = -INFINITY, L = 0.f, o = 0.f;
+        for (int t0 = 0; t0 < G.S; t0 += MG) {
+            uint64_t w[MG][3];
+#pragma unroll
+            for (int u = 0; u < MG; ++u) {
+                if (t0 + u < G.S) {
+                    const uint64_t* pp = &part[(base_item + t0 + u) * PART_WORDS];
+                    w[u][0] = ld_relaxed64(pp + 2 * HD + h);
+                    w[u][1] = ld_relaxed64(pp + 2 * HD + 2 + h);
+                    w[u][2] = ld_relaxed64(pp + j);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < MG; ++u) {
+                if (t0 + u < G.S) {
+                    const uint64_t* pp = &part[(base_item + t0 + u) * PART_WORDS];
+                    const float mt = __uint_as_float((uint32_t)(w[u][0] >> 32) == tp ? (uint32_t)w[u][0] : poll_word(c, pp + 2 * HD + h, tp, 11));
+                    const float lt = __uint_as_float((uint32_t)(w[u][1] >> 32) == tp ? (uint32_t)w[u][1] : poll_word(c, pp + 2 * HD + 2 + h, tp, 12));
+                    const float at = __uint_as_float((uint32_t)(w[u][2] >> 32) == tp ? (uint32_t)w[u][2] : poll_word(c, pp + j, tp, 12));
+                    const float Mn = fmaxf(M, mt);
+                    const float cp = expf(M - Mn), ct = expf(mt - Mn);
+                    L = L * cp + lt * ct;
+                    o = o * cp + at * ct;
+                    M = Mn;
+                }
+            }
         }
         st_tagged(&c.ws->xattn[par][G.g * 2 * HD + j], tag_of(epoch, l, E_ATTN), __float_as_uint(o / L));
     }

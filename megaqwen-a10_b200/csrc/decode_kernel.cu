@@ -818,39 +818,32 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         }
     }
     const int j0 = split_lo(2 * HD, G.S, G.s), j1 = split_lo(2 * HD, G.S, G.s + 1);
-    const int j = j0 + cs.tid;
-    if (j < j1) {
-        const int h = j >> 7;
-        const int base_item = G.g * G.S;
-        // Online merge over the splits, MG at a time: the 3 * MG tagged words of a
-        // group are loaded together (one round trip), re-read only while a tag is missing.
-        constexpr int MG = 3;
+    const int nj = j1 - j0;   // this split's slice of the pair's 256 outputs (nj * S <= 256 + S threads)
+    const int base_item = G.g * G.S;
+    // All the slice's tagged words in one round: thread k < nj * S reads acc[split t][j0 + jj],
+    // threads k < 4 S the (m, l) of (split, head); then one merge per output from shared memory.
+    consumers_sync();   // x (the warp-merge buffer) and raw are free again
+    float* sa = sm->x;    // [S][nj]
+    float* sml = sm->raw; // [S][4]: m0, m1, l0, l1
+    if (cs.tid < nj * G.S) {
+        const int t = cs.tid / nj, jj = cs.tid - t * nj;
+        sa[t * nj + jj] = __uint_as_float(poll_word(c, &part[(base_item + t) * PART_WORDS + j0 + jj], tp, 12));
+    }
+    if (cs.tid < 4 * G.S) {
+        const int t = cs.tid >> 2, q = cs.tid & 3;
+        sml[t * 4 + q] = __uint_as_float(poll_word(c, &part[(base_item + t) * PART_WORDS + 2 * HD + q], tp, 11));
+    }
+    consumers_sync();
+    if (cs.tid < nj) {
+        const int j = j0 + cs.tid, h = j >> 7;
         float M = -INFINITY, L = 0.f, o = 0.f;
-        for (int t0 = 0; t0 < G.S; t0 += MG) {
-            uint64_t w[MG][3];
-#pragma unroll
-            for (int u = 0; u < MG; ++u) {
-                if (t0 + u < G.S) {
-                    const uint64_t* pp = &part[(base_item + t0 + u) * PART_WORDS];
-                    w[u][0] = ld_relaxed64(pp + 2 * HD + h);
-                    w[u][1] = ld_relaxed64(pp + 2 * HD + 2 + h);
-                    w[u][2] = ld_relaxed64(pp + j);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < MG; ++u) {
-                if (t0 + u < G.S) {
-                    const uint64_t* pp = &part[(base_item + t0 + u) * PART_WORDS];
-                    const float mt = __uint_as_float((uint32_t)(w[u][0] >> 32) == tp ? (uint32_t)w[u][0] : poll_word(c, pp + 2 * HD + h, tp, 11));
-                    const float lt = __uint_as_float((uint32_t)(w[u][1] >> 32) == tp ? (uint32_t)w[u][1] : poll_word(c, pp + 2 * HD + 2 + h, tp, 12));
-                    const float at = __uint_as_float((uint32_t)(w[u][2] >> 32) == tp ? (uint32_t)w[u][2] : poll_word(c, pp + j, tp, 12));
-                    const float Mn = fmaxf(M, mt);
-                    const float cp = expf(M - Mn), ct = expf(mt - Mn);
-                    L = L * cp + lt * ct;
-                    o = o * cp + at * ct;
-                    M = Mn;
-                }
-            }
+        for (int t = 0; t < G.S; ++t) {
+            const float mt = sml[t * 4 + h], lt = sml[t * 4 + 2 + h], at = sa[t * nj + cs.tid];
+            const float Mn = fmaxf(M, mt);
+            const float cp = expf(M - Mn), ct = expf(mt - Mn);
+            L = L * cp + lt * ct;
+            o = o * cp + at * ct;
+            M = Mn;
         }
         st_tagged(&c.ws->xattn[par][G.g * 2 * HD + j], tag_of(epoch, l, E_ATTN), __float_as_uint(o / L));
     }

@@ -74,7 +74,15 @@ constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension
 #define MQB_ACH 16
 #endif
 constexpr int ACH = MQB_ACH;             // positions per KV chunk copy (8 or 16)
-constexpr int NBUF = 32 / ACH;           // KV chunk buffers per warp (same 16 KB per warp)
+#ifndef MQB_NBUF
+#define MQB_NBUF (32 / MQB_ACH)
+#endif
+#ifndef MQB_NAW
+#define MQB_NAW 12
+#endif
+constexpr int NBUF = MQB_NBUF;           // KV chunk buffers per attention warp
+constexpr int NAW = MQB_NAW;             // attention warps per CTA
+static_assert(NAW * NBUF * 2 * ACH * HD * 2 <= 192 * 1024, "attention buffers exceed the ring");
 constexpr int LPP = 16 / ACH;            // lanes per (head, position) for the scores
 constexpr int MAX_SPLITS_B = 130;        // partials per (sequence, KV head): 32768 / 256 + 2
 constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
@@ -132,7 +140,7 @@ struct Params {
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
 struct AttnSmem {
-    alignas(16) uint8_t kv[NW][NBUF][2 * ACH * HD * 2];   // per warp: NBUF chunks of ACH positions (K then V)
+    alignas(16) uint8_t kv[NAW][NBUF][2 * ACH * HD * 2];   // per warp: NBUF chunks of ACH positions (K then V)
     alignas(16) float q[NW][2][HD];
 };
 struct Smem {
@@ -143,7 +151,7 @@ struct Smem {
     uint64_t full[NR];       // slab copies landed
     uint64_t mdone[NR];      // MMAs reading the slot completed (tcgen05.commit)
     uint64_t deq[NR];        // slot's weights dequantised (one arrival per dequantising warp)
-    uint64_t abar[NW][NBUF]; // per-warp KV chunk copies
+    uint64_t abar[NAW][NBUF]; // per-warp KV chunk copies
     unsigned long long tokbest[BMAX];
     float rstd[BMAX];        // per-sequence 1/rms of the GEMM input being consumed
     int seqoff[BMAX + 1];    // attention work split: flattened start of each sequence
@@ -568,7 +576,7 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
     c.mma_par = 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); mbar_init(&sm->deq[i], NDQ); }
-        for (int i = 0; i < NW; ++i)
+        for (int i = 0; i < NAW; ++i)
             for (int j = 0; j < NBUF; ++j) mbar_init(&sm->abar[i][j], 1);
         sm->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -710,13 +718,19 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         const float c0 = __shfl_sync(0xffffffffu, cf, 0), c1 = __shfl_sync(0xffffffffu, cf, 16);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
-        for (int p = 0; p < n; ++p) {
+        auto pv = [&](int p) {
             const float ep0 = __shfl_sync(0xffffffffu, e, p * LPP), ep1 = __shfl_sync(0xffffffffu, e, 16 + p * LPP);
             const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * lane);
             const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
             const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
             a0[0] = fmaf(ep0, v0, a0[0]); a0[1] = fmaf(ep0, v1, a0[1]); a0[2] = fmaf(ep0, v2, a0[2]); a0[3] = fmaf(ep0, v3, a0[3]);
             a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
+        };
+        if (n == ACH) {   // full chunk: unrolled, so the shuffles and loads of all positions overlap
+#pragma unroll
+            for (int p = 0; p < ACH; ++p) pv(p);
+        } else {
+            for (int p = 0; p < n; ++p) pv(p);
         }
     };
     // cached positions [p0, p1) in ACH-position chunks, NBUF in flight per warp
@@ -825,7 +839,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         int o = 0;
         for (int t = 0; t < B; ++t) { sm->seqoff[t] = o; o += NKVH * (P.positions[t] + 1); }
         sm->seqoff[B] = o;
-        const int W = nb * NW;
+        const int W = nb * NAW;
         int q = (o + W - 1) / W;
         q = (q + 15) & ~15;
         sm->segq = q < 256 ? 256 : q;
@@ -892,7 +906,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         // ---- attention ----
         {
             const int Q = sm->segq, T = sm->seqoff[B];
-            int f = (cta * NW + warp) * Q;
+            int f = warp < NAW ? (cta * NAW + warp) * Q : T;
             const int fe = min(T, f + Q);
             int b = 0;
             while (f < fe) {
@@ -1049,7 +1063,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             if (!err) P.positions[t] += 1;
         }
     }
-    if (lane == 0)
+    if (lane == 0 && warp < NAW)
         for (int i = 0; i < NBUF; ++i)
             if (apend & (1u << i)) mbar_drain(&sm->abar[warp][i], (ause >> i) & 1u, P.budget_ns);
     drain_and_free(c);

@@ -757,13 +757,19 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         l1 = l1 * c1 + warp_sum(e1);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
-        for (int p = 0; p < n; ++p) {
+        auto pv = [&](int p) {
             const float ep0 = __shfl_sync(0xffffffffu, e0, p), ep1 = __shfl_sync(0xffffffffu, e1, p);
             const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * cs.lane);
             const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
             const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
             a0[0] = fmaf(ep0, v0, a0[0]); a0[1] = fmaf(ep0, v1, a0[1]); a0[2] = fmaf(ep0, v2, a0[2]); a0[3] = fmaf(ep0, v3, a0[3]);
             a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
+        };
+        if (n == KV_CHUNK_POS) {   // full chunk: constant trip count, so loads and shuffles overlap
+#pragma unroll 8
+            for (int p = 0; p < KV_CHUNK_POS; ++p) pv(p);
+        } else {
+            for (int p = 0; p < n; ++p) pv(p);
         }
         m0 = n0;
         m1 = n1;

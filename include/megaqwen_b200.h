@@ -174,9 +174,13 @@ int mq_decode_multi(
  * at its own position with its own KV cache, advance num_steps tokens, sharing
  * one pass over the INT8 weights per step.  The caller owns all memory: the
  * library allocates nothing on this path.
- *   - weights: INT8 projections TILE-PACKED by mq_pack_weight_tiles
- *     (LayerWeights point at the packed copies), the INT8 LM head SLAB-PACKED
- *     by mq_pack_weight_slabs, scales fp32, norms and embedding bf16;
+ *   - weights (INT8, packed by mq_pack_weight_slabs): LayerWeights.q_proj_weight
+ *     -> the q|k|v rows stacked (4096 x 1024) packed with block_k 256;
+ *     o_proj_weight and down_proj_weight packed with block_k 256;
+ *     gate_proj_weight -> gate and up pair-interleaved by 16-row tile (tile 2p =
+ *     gate rows 16p..16p+15, tile 2p+1 = the same up rows; 6144 x 1024) packed
+ *     with block_k 256; k/v/up pointers unused; the LM head packed with
+ *     block_k 64; scales (ScalePointers, unchanged) fp32, norms and embedding bf16;
  *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128];
  *   - tokens: device int32 [batch]: read as this step's inputs, overwritten
  *     with the argmax outputs (so repeated steps feed back on the device);
@@ -245,11 +249,13 @@ int mq_batch_status(const void* workspace, int* code, int* info);
  */
 int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
                          cudaStream_t stream);
-/* Same blocks, slab-major: block (kb, tile) at byte ((kb * rows/16) + tile) * 1024,
- * so consecutive row tiles of one 64-column slab are contiguous (the batched
- * LM head streams many tiles per slab with one copy). */
-int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
-                         cudaStream_t stream);
+/* Slab-major blocks of block_k (64 or 256) columns: block (kb, tile) at byte
+ * ((kb * rows/16) + tile) * 16 * block_k, inside [8-column group][16 rows][8 bytes],
+ * so the consecutive row tiles of one slab are contiguous and a CTA's rows of a
+ * slab are one copy.  The batched path uses block_k = 256 for the projections
+ * and 64 for the LM head. */
+int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int block_k,
+                         int8_t* dst, cudaStream_t stream);
 
 /*
  * The batched path's tensor-core GEMM on its own:

@@ -407,9 +407,9 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                 uint8_t* base = sm->ring + slot * SB;
                 mbar_arrive_expect_tx(&sm->full[slot], tx);
                 bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
-                if (KS == KBLK && slab_ntm > 0)   // slab-major packing: the nt tiles of this slab are contiguous
-                    bulk_g2s(base + G::A_BYTES + BB, slab_base + ((size_t)s * slab_ntm + slab_g0) * (TROWS * KBLK),
-                             nt * TROWS * KBLK, &sm->full[slot]);
+                if (slab_ntm > 0)   // slab-major packing (block width KS): the nt tiles of this slab are contiguous
+                    bulk_g2s(base + G::A_BYTES + BB, slab_base + ((size_t)s * slab_ntm + slab_g0) * (TROWS * KS),
+                             nt * TROWS * KS, &sm->full[slot]);
                 else
                     for (int j = 0; j < nt; ++j)
                         bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
@@ -506,7 +506,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
 // epi(E, ldE, g0, nt) consumes each pass's accumulator (tiles g0 .. g0 + nt).
 template <class TilePtr, class Epi>
 __device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePtr tile_ptr, Epi epi,
-                        const int8_t* slab_base = nullptr, int slab_ntm = 0) {
+                        const int8_t* slab_base = nullptr, int slab_ntm = 0, int slab_k = KBLK) {
     const int n = T1 - T0;
     if (n <= 0) return true;
     const float* E = nullptr;
@@ -518,7 +518,9 @@ __device__ bool tc_rows(Ctx& c, const uint8_t* xa, int K, int T0, int T1, TilePt
 #ifndef MQB_KSL
 #define MQB_KSL 256
 #endif
-        if (slab_ntm > 0)
+        if (slab_ntm > 0 && slab_k == 256)
+            ok = tc_gemm<256>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE, slab_base, slab_ntm, g0);
+        else if (slab_ntm > 0)
             ok = tc_gemm<64>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE, slab_base, slab_ntm, g0);
         else if (MQB_KSL >= 512 && SlabGeom<512>::A_BYTES + 3 * (g1 - g0) * TROWS * 512 <= RING / 2 && K % 512 == 0)
             ok = tc_gemm<512>(c, xa, K, g1 - g0, [&](int j) { return tile_ptr(g0 + j); }, E, ldE);
@@ -895,7 +897,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                          for (int k = 0; k < 16; ++k) v[k] = v[k] * __ldg(s_ + k) * r;
                          store16(P.qkv + (size_t)t * QKV_ROWS, row, v);
                      }
-                 }) && ok;
+                 }, wq, NTQ, 256) && ok;
         }
         stamp(P, l * 8 + 1);
         if (!grid_barrier(c, 1)) { ok = false; break; }
@@ -952,7 +954,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                  if (!(put_x8(P.xa_gu, t, row, x, XS_NORM) & put_x8(P.xa_gu, t, row + 8, x + 8, XS_NORM)))
                                      range_fail(P.ctl, 4);
                              }
-                         }) && ok;
+                         }, wo, HT, 256) && ok;
         }
         stamp(P, l * 8 + 4);
         if (!grid_barrier(c, 4)) { ok = false; break; }
@@ -962,20 +964,17 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
             const int NP = INTER / TROWS;
             const int P0 = split_lo(NP, nb, cta), np = split_lo(NP, nb, cta + 1) - P0;
             const int8_t* wg = (const int8_t*)w.gate_proj_weight;
-            const int8_t* wu = (const int8_t*)w.up_proj_weight;
             const float* sg = sc.gate_scale; const float* su = sc.up_scale;
-            // tiles [0, np): gate rows, [np, 2 np): the matching up rows (one pass: np <= 2)
-            ok = tc_rows(c, P.xa_gu, HIDDEN, 0, 2 * np,
-                         [&](int j) {
-                             return j < np ? wg + (size_t)(P0 + j) * TROWS * HIDDEN
-                                           : wu + (size_t)(P0 + j - np) * TROWS * HIDDEN;
-                         },
+            // fused gate/up matrix, pair-interleaved: tile 2p = gate rows of pair p, 2p + 1 = up rows
+            // (one pass: np <= 2); this CTA's pairs are the contiguous tiles [2 P0, 2 P0 + 2 np)
+            ok = tc_rows(c, P.xa_gu, HIDDEN, 2 * P0, 2 * (P0 + np),
+                         [&](int g) { return wg + (size_t)g * TROWS * HIDDEN; },
                          [&](const float* E, int ldE, int, int) {
                              for (int i = threadIdx.x; i < B * np; i += NT) {
                                  const int t = i % B, jp = i / B, row = TROWS * (P0 + jp);
                                  float gv[16], uv[16], m[16];
-                                 erow16(E, ldE, t, TROWS * jp, 1.0f / XS_NORM, gv);
-                                 erow16(E, ldE, t, TROWS * (np + jp), 1.0f / XS_NORM, uv);
+                                 erow16(E, ldE, t, TROWS * (2 * jp), 1.0f / XS_NORM, gv);
+                                 erow16(E, ldE, t, TROWS * (2 * jp + 1), 1.0f / XS_NORM, uv);
                                  const float r = sm->rstd[t];
 #pragma unroll
                                  for (int k = 0; k < 16; ++k) {
@@ -986,7 +985,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                  if (!(put_x8(P.xa_dn, t, row, m, XS_ACT) & put_x8(P.xa_dn, t, row + 8, m + 8, XS_ACT)))
                                      range_fail(P.ctl, 5);
                              }
-                         }) && ok;
+                         }, wg, 2 * NP, 256) && ok;
         }
         stamp(P, l * 8 + 5);
         if (!grid_barrier(c, 5)) { ok = false; break; }
@@ -1016,7 +1015,7 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                  if (!(put_x8(P.xa_qkv, t, row, x, XS_NORM) & put_x8(P.xa_qkv, t, row + 8, x + 8, XS_NORM)))
                                      range_fail(P.ctl, 6);
                              }
-                         }) && ok;
+                         }, wd, HT, 256) && ok;
         }
         stamp(P, l * 8 + 6);
         if (!grid_barrier(c, 6)) { ok = false; break; }
@@ -1126,17 +1125,18 @@ __global__ void __launch_bounds__(NT, 1) matmul_kernel(const MMParams Q) {
     drain_and_free(c);
 }
 
-// INT8 [rows][K] -> slab-major packed blocks: block (kb, tile) at
-// ((kb * rows/16) + tile) * 1024, inside [8-k column][16 rows][8 bytes].
-__global__ void pack_slabs_kernel(const int8_t* src, int64_t rows, int K, int64_t src_stride, int8_t* dst) {
+// INT8 [rows][K] -> slab-major packed blocks of bk columns: block (kb, tile) at
+// ((kb * rows/16) + tile) * 16 * bk, inside [8-k column][16 rows][8 bytes].
+__global__ void pack_slabs_kernel(const int8_t* src, int64_t rows, int K, int64_t src_stride, int bk, int8_t* dst) {
     const int64_t n = rows * (K / 8);
     const int64_t ntiles = rows / TROWS;
+    const int U = 2 * bk;   // 8-byte units per block
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t blk = i >> 7;
-        const int u = (int)(i & 127), kc = u >> 4, r = u & 15;
+        const int64_t blk = i / U;
+        const int u = (int)(i - blk * U), kc = u >> 4, r = u & 15;
         const int kb = (int)(blk / ntiles);
         const int64_t tile = blk - (int64_t)kb * ntiles;
-        const int8_t* s = src + (tile * TROWS + r) * src_stride + kb * KBLK + kc * 8;
+        const int8_t* s = src + (tile * TROWS + r) * src_stride + (int64_t)kb * bk + kc * 8;
         uint2 v;
         memcpy(&v, s, 8);
         *reinterpret_cast<uint2*>(dst + i * 8) = v;
@@ -1233,15 +1233,15 @@ extern "C" int mq_pack_weight_tiles(const int8_t* src, int64_t rows, int K, int6
     return (int)cudaGetLastError();
 }
 
-extern "C" int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int8_t* dst,
-                                    cudaStream_t stream) {
+extern "C" int mq_pack_weight_slabs(const int8_t* src, int64_t rows, int K, int64_t src_row_stride, int block_k,
+                                    int8_t* dst, cudaStream_t stream) {
     using namespace batch;
-    if (!src || !dst || rows <= 0 || K <= 0) return MQ_ERR_ARG;
-    if (rows % TROWS != 0 || K % KBLK != 0 || src_row_stride < K || src_row_stride % 8 != 0) return MQ_ERR_SIZE;
+    if (!src || !dst || rows <= 0 || K <= 0 || (block_k != 64 && block_k != 256)) return MQ_ERR_ARG;
+    if (rows % TROWS != 0 || K % block_k != 0 || src_row_stride < K || src_row_stride % 8 != 0) return MQ_ERR_SIZE;
     if (((uintptr_t)src & 7u) != 0 || !al16(dst)) return MQ_ERR_ARG;
     const int64_t units = rows * (K / 8);
     const int grid = (int)((units + 255) / 256 < 65536 ? (units + 255) / 256 : 65536);
-    pack_slabs_kernel<<<grid, 256, 0, stream>>>(src, rows, K, src_row_stride, dst);
+    pack_slabs_kernel<<<grid, 256, 0, stream>>>(src, rows, K, src_row_stride, block_k, dst);
     return (int)cudaGetLastError();
 }
 

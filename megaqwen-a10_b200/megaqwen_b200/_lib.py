@@ -73,7 +73,7 @@ def load():
     lib.mq_batch_decode.argtypes = [_vp, _i, _vp]
     lib.mq_batch_status.argtypes = [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]
     lib.mq_pack_weight_tiles.argtypes = [_vp, _i64, _i, _i64, _vp, _vp]
-    lib.mq_pack_weight_slabs.argtypes = [_vp, _i64, _i, _i64, _vp, _vp]
+    lib.mq_pack_weight_slabs.argtypes = [_vp, _i64, _i, _i64, _i, _vp, _vp]
     lib.mq_batch_matmul_workspace_bytes.argtypes = [_i, ctypes.POINTER(ctypes.c_size_t)]
     lib.mq_batch_matmul.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, ctypes.c_size_t, _vp]
     lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]

@@ -33,19 +33,23 @@ class MQBatchArgs(ctypes.Structure):
     ]
 
 
-def pack_tiles(w, slab_major=False):
-    """INT8 [rows, K] (rows % 16 == 0, K % 64 == 0) -> packed copy (same bytes, 16-row x
-    64-column 1 KB blocks): tile-major (mq_pack_weight_tiles, the projections) or
-    slab-major (mq_pack_weight_slabs, the LM head)."""
+def pack_tiles(w, slab_major=False, block_k=64):
+    """INT8 [rows, K] (rows % 16 == 0, K % block_k == 0) -> packed copy (same bytes):
+    tile-major 16-row x 64-column 1 KB blocks (mq_pack_weight_tiles, the stand-alone
+    GEMM) or slab-major 16-row x block_k blocks (mq_pack_weight_slabs: the batched
+    decode's projections with block_k 256, its LM head with 64)."""
     if w.dtype != torch.int8 or w.dim() != 2 or not w.is_cuda or not w.is_contiguous():
         raise ValueError("pack_tiles: contiguous CUDA int8 [rows, K] expected")
     out = torch.empty_like(w)
     lib = _lib.load()
-    fn = lib.mq_pack_weight_slabs if slab_major else lib.mq_pack_weight_tiles
     with torch.cuda.device(w.device):
-        stream = torch.cuda.current_stream(w.device).cuda_stream
-        _lib.check(fn(ctypes.c_void_p(w.data_ptr()), w.shape[0], w.shape[1], w.shape[1],
-                      ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream)), "pack_tiles")
+        stream = ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)
+        src, dst = ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(out.data_ptr())
+        if slab_major:
+            rc = lib.mq_pack_weight_slabs(src, w.shape[0], w.shape[1], w.shape[1], int(block_k), dst, stream)
+        else:
+            rc = lib.mq_pack_weight_tiles(src, w.shape[0], w.shape[1], w.shape[1], dst, stream)
+        _lib.check(rc, "pack_tiles")
     return out
 
 
@@ -83,13 +87,21 @@ def packed_weights(dec):
         keep = []
         arr = (_lib.LayerWeights * dec.num_layers_)()
         flat = dec.layer_weights_flat_
+        names = [f for f, _ in _lib.LayerWeights._fields_]
         for i in range(dec.num_layers_):
-            for j, (fname, _) in enumerate(_lib.LayerWeights._fields_):
-                t = flat[i * 11 + j]
-                if t.dim() == 2:
-                    t = pack_tiles(t)
-                    keep.append(t)
-                setattr(arr[i], fname, t.data_ptr())
+            t = {n: flat[i * 11 + j] for j, n in enumerate(names)}
+            qkv = pack_tiles(torch.cat([t["q_proj_weight"], t["k_proj_weight"], t["v_proj_weight"]], 0).contiguous(),
+                             slab_major=True, block_k=256)
+            g, u = t["gate_proj_weight"], t["up_proj_weight"]
+            gu = torch.stack([g.view(-1, 16, g.shape[1]), u.view(-1, 16, u.shape[1])], 1).reshape(-1, g.shape[1])
+            gu = pack_tiles(gu.contiguous(), slab_major=True, block_k=256)
+            o = pack_tiles(t["o_proj_weight"], slab_major=True, block_k=256)
+            d = pack_tiles(t["down_proj_weight"], slab_major=True, block_k=256)
+            keep += [qkv, gu, o, d]
+            packed = {"q_proj_weight": qkv, "k_proj_weight": qkv, "v_proj_weight": qkv, "o_proj_weight": o,
+                      "gate_proj_weight": gu, "up_proj_weight": gu, "down_proj_weight": d}
+            for n in names:
+                setattr(arr[i], n, packed.get(n, t[n]).data_ptr())
         table = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).to(dec.device)
         lm = pack_tiles(dec.lm_head_weight_, slab_major=True)
         pk = dec._packed_ = (table, lm, keep)

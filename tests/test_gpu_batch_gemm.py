@@ -60,3 +60,16 @@ def test_pack_slabs_layout():
                 for r in range(16):
                     off = ((kb * 2 + tile) * 1024) + kc * 128 + r * 8
                     assert torch.equal(p[off:off + 8], wc[tile * 16 + r, kb * 64 + kc * 8: kb * 64 + kc * 8 + 8])
+
+
+def test_pack_slabs_256_layout():
+    w = torch.randint(-128, 128, (48, 512), device="cuda", dtype=torch.int32).to(torch.int8)
+    p = mq.pack_tiles(w, slab_major=True, block_k=256).cpu().view(-1)
+    wc = w.cpu()
+    # block (kb, tile) at ((kb * rows/16) + tile) * 16 * 256, inside [8-col group][16 rows][8 bytes]
+    for tile in range(3):
+        for kb in range(2):
+            for kc in range(32):
+                for r in (0, 7, 15):
+                    off = ((kb * 3 + tile) * 4096) + kc * 128 + r * 8
+                    assert torch.equal(p[off:off + 8], wc[tile * 16 + r, kb * 256 + kc * 8: kb * 256 + kc * 8 + 8])

@@ -75,3 +75,9 @@ def test_batched_rejects_bad_input_on_device():
     out = bd.step(1).cpu().tolist()
     assert out == [-1, -1]
     assert bd.status()[0] == 4
+
+
+def test_batched_long_context_and_single_sequence():
+    # one sequence deep in a long cache (many attention pieces per head) next to a short one
+    _compare(L=2, positions=[20000, 3], tokens=[11, 22], steps=2, max_seq=20480)
+    _compare(L=2, positions=[1500], tokens=[99], steps=2, max_seq=2048)

@@ -16,7 +16,10 @@
 //   GU    gate and up GEMM, SiLU(gate)*up -> DOWN operand
 //   DOWN  GEMM + residual -> h (rounded to bf16, as between layers of the
 //         batch-1 kernel), next QKV (or LM-head) operand
-// then the LM-head GEMM with a per-sequence packed argmax.
+// then the LM-head GEMM with a per-sequence packed argmax.  Prefill mode
+// (rows = consecutive tokens of one sequence sharing its cache) adds a K/V
+// write sub-phase and a barrier before attention; vocab-sharded mode scores
+// one slice of the vocabulary and emits packed argmax keys.
 //
 // GEMM shape.  D[128 x N] = X[128 x K] * W[N x K]^T: rows 0..63 of X are the
 // 64 sequences' activations as fp16 of x * 2^-s (rows 64..127 are don't-care
@@ -26,10 +29,11 @@
 //   * the activation operand lives in global memory already in the tensor
 //     core's K-major no-swizzle layout (8-wide k columns of [64 rows][16 B]),
 //     written by the producing phase's epilogue, so a slab is ONE bulk copy;
-//   * the INT8 weights are tile-packed once at load time (16 rows x 64 k per
-//     1 KB block, in [8-k column][row][8 B] order), so a slab of a tile is one
-//     bulk copy; the CTA dequantises it to fp16 (exact) in shared memory in the
-//     same K-major layout and one thread issues the tcgen05.mma instructions;
+//   * the INT8 weights are packed once at load time slab-major (blocks of 16
+//     rows x 256 k for the projections, 16 x 64 for the LM head, [8-k
+//     column][row][8 B] inside), so this CTA's rows of a slab are one bulk
+//     copy; the CTA dequantises them to fp16 (exact) in shared memory in the
+//     same K-major layout and two threads issue the tcgen05.mma instructions;
 //   * the per-row weight scale, 2^s and, for RMSNorm inputs, the per-sequence
 //     1/rms multiply the fp32 accumulator in the epilogue, read back from TMEM
 //     with tcgen05.ld.
@@ -98,7 +102,7 @@ static_assert(3 * (BMAX * 64 * 2 + 3 * 256 * 64) <= RING, "ring too small for th
 static_assert(2 * (BMAX * 128 * 2 + 3 * 80 * 128) <= RING, "ring too small for two N = 80 slabs");
 
 struct Params {
-    // weights: INT8 matrices tile-packed (mq_pack_weight_tiles)
+    // weights: INT8 matrices packed slab-major (mq_pack_weight_slabs; see MQBatchArgs)
     const __nv_bfloat16* embed;
     const LayerWeights* layers;
     const ScalePointers* scales;

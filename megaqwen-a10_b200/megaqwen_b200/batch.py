@@ -80,7 +80,8 @@ def batch_matmul(w_tiles, scale, x):
 
 
 def packed_weights(dec):
-    """(device LayerWeights table of the tile-packed projections, slab-packed LM
+    """(device LayerWeights table of the slab-packed projections (q|k|v fused, gate/up
+    interleaved), slab-packed LM
     head) of an A10Int8MegakernelDecoder, built once and kept on the decoder."""
     pk = getattr(dec, "_packed_", None)
     if pk is None:
@@ -203,7 +204,7 @@ class BatchedDecoder:
     MAX_BATCH = 64
 
     def __init__(self, weights, batch, max_seq_len, vocab_shard=None):
-        """weights: an A10Int8MegakernelDecoder (its INT8 matrices are tile-packed here);
+        """weights: an A10Int8MegakernelDecoder (its INT8 matrices are packed here, once per decoder);
         max_seq_len <= 32768 and <= the rows of its RoPE tables.
         vocab_shard: (rank, world, dist, group) to split the LM head over `world`
         ranks that decode the SAME sequences (same tokens and caches on every

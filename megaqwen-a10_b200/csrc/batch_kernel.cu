@@ -51,6 +51,8 @@ constexpr int NW = 12;                   // warps per CTA
 constexpr int NT = NW * 32;
 constexpr int MROWS = 128;               // MMA M (rows 0..63: the sequences; 64..127 unused)
 constexpr int XCOL = BMAX * 16;          // bytes of one 8-wide k column of the activation operand
+constexpr int HROWS = BMAX / 2;          // token-half operands (O, down): 32 rows
+constexpr int HXCOL = HROWS * 16;        // bytes of one 8-wide k column of a token-half operand
 // Activation operands are stored as fp16 of x * 2^-s (exact power-of-two
 // pre-scale, undone in the epilogue): s = 8 for RMSNorm inputs (h * w, which
 // carry the residual stream's magnitude), 4 for attention and MLP outputs.
@@ -174,6 +176,7 @@ struct Ctx {
     uint32_t pend;           // ring slots with copies issued and not known complete (producer)
     uint32_t ppar;           // bit i: parity of the last copy issued into slot i
     int mma_slot;            // slot of the last commit nobody waited for (-1: none)
+    int half;                // -1: the operand holds all 64 sequences; 0 / 1: token-half operand (32 rows)
     uint32_t mma_par;
 };
 
@@ -304,10 +307,9 @@ __device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t v) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Writes x[0..7] * sc (k0 .. k0 + 7 of sequence t, k0 % 8 == 0) into an
-// activation operand as fp16 (row t of the 8-wide k column).  Returns false if
-// a value is outside the fp16 range (or not finite).
-__device__ __forceinline__ bool put_x8(uint8_t* xa, int t, int k0, const float* x, float sc) {
+// x[0..7] * sc as eight fp16 (one 16-byte row of an 8-wide k column); false if a
+// value is outside the fp16 range (or not finite).
+__device__ __forceinline__ bool pack_x8(const float* x, float sc, uint4& out) {
     uint32_t w[4];
     bool ok = true;
 #pragma unroll
@@ -317,7 +319,23 @@ __device__ __forceinline__ bool put_x8(uint8_t* xa, int t, int k0, const float* 
         const __half2 h = __floats2half2_rn(a, b);
         w[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    *reinterpret_cast<uint4*>(xa + (size_t)(k0 >> 3) * XCOL + t * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    out = make_uint4(w[0], w[1], w[2], w[3]);
+    return ok;
+}
+// Writes x[0..7] * sc (k0 .. k0 + 7 of sequence t, k0 % 8 == 0) into an
+// activation operand as fp16 (row t of the 8-wide k column).
+__device__ __forceinline__ bool put_x8(uint8_t* xa, int t, int k0, const float* x, float sc) {
+    uint4 v;
+    const bool ok = pack_x8(x, sc, v);
+    *reinterpret_cast<uint4*>(xa + (size_t)(k0 >> 3) * XCOL + t * 16) = v;
+    return ok;
+}
+// The same into a token-half operand of K columns: [half][k column][32 rows][16 B].
+__device__ __forceinline__ bool put_x8h(uint8_t* xa, int K, int t, int k0, const float* x, float sc) {
+    uint4 v;
+    const bool ok = pack_x8(x, sc, v);
+    *reinterpret_cast<uint4*>(xa + (size_t)(t / HROWS) * (K / 8) * HXCOL + (size_t)(k0 >> 3) * HXCOL +
+                              (t % HROWS) * 16) = v;
     return ok;
 }
 __device__ __noinline__ void range_fail(unsigned* ctl, int where) {
@@ -393,8 +411,12 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int N = nt * TROWS, S = K / KS;
     const int BB = 2 * N * KS, BR = N * KS;
-    const uint32_t tx = (uint32_t)(G::A_BYTES + BR);
-    const int SB = G::slot_bytes(N);
+    // activation operand: 64 rows, or (token-half operands, stored [half][k column][32 rows][16 B]) 32 rows
+    const int XC = c.half >= 0 ? HXCOL : XCOL;
+    const int AB = XC / 16 * KS * 2;
+    const uint8_t* xs = xa + (c.half >= 0 ? (size_t)c.half * (K / 8) * HXCOL : 0);
+    const uint32_t tx = (uint32_t)(AB + BR);
+    const int SB = (AB + 3 * N * KS + 1023) & ~1023;
     const int nr = min(NR, RING / SB);
     const uint32_t par0 = c.upar;   // parity of the next use of each slot
     // parity of the mbarrier phases of slab s (its slot's (s / nr)-th use in this GEMM)
@@ -410,13 +432,13 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                 }
                 uint8_t* base = sm->ring + slot * SB;
                 mbar_arrive_expect_tx(&sm->full[slot], tx);
-                bulk_g2s(base, xa + (size_t)s * G::A_BYTES, G::A_BYTES, &sm->full[slot]);
+                bulk_g2s(base, xs + (size_t)s * AB, AB, &sm->full[slot]);
                 if (slab_ntm > 0)   // slab-major packing (block width KS): the nt tiles of this slab are contiguous
-                    bulk_g2s(base + G::A_BYTES + BB, slab_base + ((size_t)s * slab_ntm + slab_g0) * (TROWS * KS),
+                    bulk_g2s(base + AB + BB, slab_base + ((size_t)s * slab_ntm + slab_g0) * (TROWS * KS),
                              nt * TROWS * KS, &sm->full[slot]);
                 else
                     for (int j = 0; j < nt; ++j)
-                        bulk_g2s(base + G::A_BYTES + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
+                        bulk_g2s(base + AB + BB + j * TROWS * KS, tile_ptr(j) + (size_t)s * TROWS * KS,
                                  TROWS * KS, &sm->full[slot]);
                 c.pend |= 1u << slot;
                 c.ppar = (c.ppar & ~(1u << slot)) | (par(s) << slot);
@@ -434,10 +456,10 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
                      mbar_wait_b(c, &sm->deq[slot], par(s), 240 + slot);     // weights dequantised
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sm->ring + slot * SB), b0 = a0 + G::A_BYTES;
+                const uint32_t a0 = smem_u32(sm->ring + slot * SB), b0 = a0 + AB;
 #pragma unroll
                 for (int i = 0; i < KS / 16; ++i)
-                    umma_f16(acc, sdesc(a0 + i * 2 * XCOL, XCOL, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128), idesc,
+                    umma_f16(acc, sdesc(a0 + i * 2 * XC, XC, 128), sdesc(b0 + i * 2 * N * 16, N * 16, 128), idesc,
                              (s >= NMMA || i != 0));
                 umma_commit(&sm->mdone[slot]);
                 c.mma_slot = slot;
@@ -451,7 +473,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
             const int slot = s % nr;
             ok = mbar_wait_b(c, &sm->full[slot], par(s), 210 + slot);
             if (!ok) break;
-            uint8_t* bb = sm->ring + slot * SB + G::A_BYTES;
+            uint8_t* bb = sm->ring + slot * SB + AB;
             const uint8_t* raw = bb + BB;
             // item (kc, n): 8 int8 -> one 16-byte row of a core matrix
             // item i = kc * N + n walks by 32 * NDQ: (kc, n) advanced without a division
@@ -485,7 +507,7 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     float* Ew = reinterpret_cast<float*>(sm->ring);
     ldE = N + 4;
     const int q = warp & 3;   // tcgen05.ld: warp w reaches TMEM lanes 32 (w % 4) .. + 31; rows 0..63 only
-    for (int c8 = q < 2 ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
+    for (int c8 = q < XC / 512 ? warp >> 2 : N / 8; c8 < N / 8; c8 += NW / 4) {
         float v[8];
         tmem_ld8(c.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(c8 * 8), v);
 #pragma unroll
@@ -580,6 +602,7 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
     c.ppar = 0;
     c.mma_slot = -1;
     c.mma_par = 0;
+    c.half = -1;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) { mbar_init(&sm->full[i], 1); mbar_init(&sm->mdone[i], 1); mbar_init(&sm->deq[i], NDQ); }
         for (int i = 0; i < NAW; ++i)
@@ -818,7 +841,8 @@ __device__ void merge_item(const Smem* sm, const Params& P, int b, int qh) {
         w[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
     const int k0 = qh * HD + 4 * lane;
-    *reinterpret_cast<uint2*>(P.xa_o + (size_t)(k0 >> 3) * XCOL + b * 16 + (k0 & 7) * 2) = make_uint2(w[0], w[1]);
+    *reinterpret_cast<uint2*>(P.xa_o + (size_t)(b / HROWS) * (QSZ / 8) * HXCOL + (size_t)(k0 >> 3) * HXCOL +
+                              (b % HROWS) * 16 + (k0 & 7) * 2) = make_uint2(w[0], w[1]);
     if (!ok) range_fail(P.ctl, 3);
 }
 
@@ -934,31 +958,39 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
         stamp(P, l * 8 + 3);
         if (!grid_barrier(c, 3)) { ok = false; break; }
         // ---- O + residual -> act, GU operand ----
+        // Units (16-row tile g, token half h): each CTA reads the half of the operand
+        // it needs, and 128 CTAs share the work instead of 64.
         {
-            const int T0 = split_lo(HT, nb, cta), T1 = split_lo(HT, nb, cta + 1);
+            const int U0 = split_lo(2 * HT, nb, cta), U1 = split_lo(2 * HT, nb, cta + 1);
             const int8_t* wo = (const int8_t*)w.o_proj_weight;
             const __nv_bfloat16* pw = (const __nv_bfloat16*)w.post_attn_layernorm_weight;
             const float* so = sc.o_scale;
-            ok = tc_rows(c, P.xa_o, QSZ, T0, T1, [&](int g) { return wo + (size_t)g * TROWS * QSZ; },
-                         [&](const float* E, int ldE, int g0, int nt) {
-                             for (int i = threadIdx.x; i < B * nt; i += NT) {
-                                 const int t = i % B, g = g0 + i / B, row = TROWS * g;
-                                 float v[16], hv[16], wv[16], x[16], ss = 0.f;
-                                 erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_ACT, v);
-                                 load16(P.h + (size_t)t * HIDDEN, row, hv);
-                                 load16_bf16(pw, row, wv);
+            for (int u = U0; u < U1 && ok; ++u) {
+                const int g = u >> 1, h = u & 1, nt_h = min(HROWS, B - h * HROWS);
+                if (nt_h <= 0) continue;
+                c.half = h;
+                ok = tc_rows(c, P.xa_o, QSZ, g, g + 1, [&](int gg) { return wo + (size_t)gg * TROWS * QSZ; },
+                             [&](const float* E, int ldE, int, int) {
+                                 for (int r = threadIdx.x; r < nt_h; r += NT) {
+                                     const int t = h * HROWS + r, row = TROWS * g;
+                                     float v[16], hv[16], wv[16], x[16], ss = 0.f;
+                                     erow16(E, ldE, r, 0, 1.0f / XS_ACT, v);
+                                     load16(P.h + (size_t)t * HIDDEN, row, hv);
+                                     load16_bf16(pw, row, wv);
 #pragma unroll
-                                 for (int k = 0; k < 16; ++k) {
-                                     v[k] = v[k] * __ldg(so + row + k) + hv[k];
-                                     ss += v[k] * v[k];
-                                     x[k] = v[k] * wv[k];
+                                     for (int k = 0; k < 16; ++k) {
+                                         v[k] = v[k] * __ldg(so + row + k) + hv[k];
+                                         ss += v[k] * v[k];
+                                         x[k] = v[k] * wv[k];
+                                     }
+                                     store16(P.act + (size_t)t * HIDDEN, row, v);
+                                     P.ss_b[g * BMAX + t] = ss;
+                                     if (!(put_x8(P.xa_gu, t, row, x, XS_NORM) & put_x8(P.xa_gu, t, row + 8, x + 8, XS_NORM)))
+                                         range_fail(P.ctl, 4);
                                  }
-                                 store16(P.act + (size_t)t * HIDDEN, row, v);
-                                 P.ss_b[g * BMAX + t] = ss;
-                                 if (!(put_x8(P.xa_gu, t, row, x, XS_NORM) & put_x8(P.xa_gu, t, row + 8, x + 8, XS_NORM)))
-                                     range_fail(P.ctl, 4);
-                             }
-                         }, wo, HT, 256) && ok;
+                             }, wo, HT, 256) && ok;
+                c.half = -1;
+            }
         }
         stamp(P, l * 8 + 4);
         if (!grid_barrier(c, 4)) { ok = false; break; }
@@ -986,40 +1018,46 @@ __global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
                                      const float ud = uv[k] * __ldg(su + row + k) * r;
                                      m[k] = gd / (1.0f + expf(-gd)) * ud;
                                  }
-                                 if (!(put_x8(P.xa_dn, t, row, m, XS_ACT) & put_x8(P.xa_dn, t, row + 8, m + 8, XS_ACT)))
+                                 if (!(put_x8h(P.xa_dn, INTER, t, row, m, XS_ACT) & put_x8h(P.xa_dn, INTER, t, row + 8, m + 8, XS_ACT)))
                                      range_fail(P.ctl, 5);
                              }
                          }, wg, 2 * NP, 256) && ok;
         }
         stamp(P, l * 8 + 5);
         if (!grid_barrier(c, 5)) { ok = false; break; }
-        // ---- down + residual -> h, next QKV (or LM-head) operand ----
+        // ---- down + residual -> h, next QKV (or LM-head) operand (units as for O) ----
         {
-            const int T0 = split_lo(HT, nb, cta), T1 = split_lo(HT, nb, cta + 1);
+            const int U0 = split_lo(2 * HT, nb, cta), U1 = split_lo(2 * HT, nb, cta + 1);
             const int8_t* wd = (const int8_t*)w.down_proj_weight;
             const float* sd = sc.down_scale;
             const __nv_bfloat16* nn =
                 l + 1 < P.L ? (const __nv_bfloat16*)P.layers[l + 1].input_layernorm_weight : P.final_norm;
-            ok = tc_rows(c, P.xa_dn, INTER, T0, T1, [&](int g) { return wd + (size_t)g * TROWS * INTER; },
-                         [&](const float* E, int ldE, int g0, int nt) {
-                             for (int i = threadIdx.x; i < B * nt; i += NT) {
-                                 const int t = i % B, g = g0 + i / B, row = TROWS * g;
-                                 float v[16], av[16], wv[16], x[16], ss = 0.f;
-                                 erow16(E, ldE, t, TROWS * (g - g0), 1.0f / XS_ACT, v);
-                                 load16(P.act + (size_t)t * HIDDEN, row, av);
-                                 load16_bf16(nn, row, wv);
+            for (int u = U0; u < U1 && ok; ++u) {
+                const int g = u >> 1, h = u & 1, nt_h = min(HROWS, B - h * HROWS);
+                if (nt_h <= 0) continue;
+                c.half = h;
+                ok = tc_rows(c, P.xa_dn, INTER, g, g + 1, [&](int gg) { return wd + (size_t)gg * TROWS * INTER; },
+                             [&](const float* E, int ldE, int, int) {
+                                 for (int r = threadIdx.x; r < nt_h; r += NT) {
+                                     const int t = h * HROWS + r, row = TROWS * g;
+                                     float v[16], av[16], wv[16], x[16], ss = 0.f;
+                                     erow16(E, ldE, r, 0, 1.0f / XS_ACT, v);
+                                     load16(P.act + (size_t)t * HIDDEN, row, av);
+                                     load16_bf16(nn, row, wv);
 #pragma unroll
-                                 for (int k = 0; k < 16; ++k) {
-                                     v[k] = bf16r(v[k] * __ldg(sd + row + k) + av[k]);
-                                     ss += v[k] * v[k];
-                                     x[k] = v[k] * wv[k];
+                                     for (int k = 0; k < 16; ++k) {
+                                         v[k] = bf16r(v[k] * __ldg(sd + row + k) + av[k]);
+                                         ss += v[k] * v[k];
+                                         x[k] = v[k] * wv[k];
+                                     }
+                                     store16(P.h + (size_t)t * HIDDEN, row, v);
+                                     P.ss_a[g * BMAX + t] = ss;
+                                     if (!(put_x8(P.xa_qkv, t, row, x, XS_NORM) & put_x8(P.xa_qkv, t, row + 8, x + 8, XS_NORM)))
+                                         range_fail(P.ctl, 6);
                                  }
-                                 store16(P.h + (size_t)t * HIDDEN, row, v);
-                                 P.ss_a[g * BMAX + t] = ss;
-                                 if (!(put_x8(P.xa_qkv, t, row, x, XS_NORM) & put_x8(P.xa_qkv, t, row + 8, x + 8, XS_NORM)))
-                                     range_fail(P.ctl, 6);
-                             }
-                         }, wd, HT, 256) && ok;
+                             }, wd, HT, 256) && ok;
+                c.half = -1;
+            }
         }
         stamp(P, l * 8 + 6);
         if (!grid_barrier(c, 6)) { ok = false; break; }

@@ -41,6 +41,8 @@
 // with per-16-row partial sums of squares; the consumer reduces the 64 partials
 // in a fixed order, so results are deterministic.
 #include "common.cuh"
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdlib.h>
 
 namespace mq {
@@ -76,12 +78,9 @@ constexpr int ACC_COLS = 256;            // fp32 accumulator columns (N <= 256)
 constexpr int TMEM_COLS = NMMA == 1 ? 256 : 512;   // one accumulator per MMA issuer
 constexpr int MAX_TILES_PASS = ACC_COLS / TROWS;
 constexpr int HT = HIDDEN / TROWS;       // 64 row tiles of the hidden dimension (sum-of-squares partials)
-#ifndef MQB_ACH
-#define MQB_ACH 16
-#endif
-constexpr int ACH = MQB_ACH;             // positions per KV chunk copy (8 or 16)
+constexpr int ACH = 16;                  // positions per KV chunk (one m16n8k16 tile of positions)
 #ifndef MQB_NBUF
-#define MQB_NBUF (32 / MQB_ACH)
+#define MQB_NBUF 2
 #endif
 #ifndef MQB_NAW
 #define MQB_NAW 12
@@ -89,7 +88,6 @@ constexpr int ACH = MQB_ACH;             // positions per KV chunk copy (8 or 16
 constexpr int NBUF = MQB_NBUF;           // KV chunk buffers per attention warp
 constexpr int NAW = MQB_NAW;             // attention warps per CTA
 static_assert(NAW * NBUF * 2 * ACH * HD * 2 <= 192 * 1024, "attention buffers exceed the ring");
-constexpr int LPP = 16 / ACH;            // lanes per (head, position) for the scores
 constexpr int MAX_SPLITS_B = 130;        // partials per (sequence, KV head): 32768 / 256 + 2
 constexpr int PARTW = 2 * HD + 4;        // acc[2][128], m[2], l[2]
 
@@ -104,6 +102,9 @@ static_assert(3 * (BMAX * 64 * 2 + 3 * 256 * 64) <= RING, "ring too small for th
 static_assert(2 * (BMAX * 128 * 2 + 3 * 80 * 128) <= RING, "ring too small for two N = 80 slabs");
 
 struct Params {
+    // K / V caches as 2-D tensors [rows = B * L * 8 * max_seq][128] bf16, box 16 rows x 64 dims, 128-byte
+    // swizzle: the attention warps fetch 16-position chunks with TMA so that ldmatrix reads them conflict-free
+    CUtensorMap tm_k, tm_v;
     // weights: INT8 matrices packed slab-major (mq_pack_weight_slabs; see MQBatchArgs)
     const __nv_bfloat16* embed;
     const LayerWeights* layers;
@@ -146,12 +147,12 @@ struct Params {
 // Shared memory (phases use disjoint views of one buffer)
 // ---------------------------------------------------------------------------
 struct AttnSmem {
-    alignas(16) uint8_t kv[NAW][NBUF][2 * ACH * HD * 2];   // per warp: NBUF chunks of ACH positions (K then V)
+    alignas(1024) uint8_t kv[NAW][NBUF][2 * ACH * HD * 2];   // per warp: NBUF chunks of ACH positions (K then V)
     alignas(16) float q[NW][2][HD];
 };
 struct Smem {
     union {
-        alignas(128) uint8_t ring[RING];          // GEMM slab slots; after the last MMA, the fp32 epilogue tile
+        alignas(1024) uint8_t ring[RING];         // GEMM slab slots; after the last MMA, the fp32 epilogue tile
         AttnSmem a;
     };
     uint64_t full[NR];       // slab copies landed
@@ -165,6 +166,8 @@ struct Smem {
     uint32_t tmem_base;
     int abort_flag;
 };
+
+static_assert(sizeof(Smem) + 1024 <= 227 * 1024, "shared memory (plus the alignment KB) exceeds 227 KB");
 
 struct Ctx {
     Smem* sm;
@@ -616,6 +619,34 @@ __device__ void init_ctx(Ctx& c, Smem* sm, unsigned* ctl, unsigned long long bud
 }
 
 // ---------------------------------------------------------------------------
+// Warp-level bf16 MMA pieces for the attention products
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&a)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&a)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]) : "r"(addr) : "memory");
+}
+// Two floats as bf16x2 (part 0: the bf16 of x; part 1: the bf16 of the remainder).
+__device__ __forceinline__ uint32_t bf2_part(float x, float y, int part) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    if (part) {
+        const float2 f = __bfloat1622float2(h);
+        h = __floats2bfloat162_rn(x - f.x, y - f.y);
+    }
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------------------
 // Attention: one warp per (sequence, KV head, split)
 // ---------------------------------------------------------------------------
 // Work split: the (sequence, KV head, position) triples of a step, flattened
@@ -702,77 +733,114 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         }
     }
     __syncwarp();
-    // Scores: lane = (head hq of the pair, position pl of the chunk, part hf of
-    // the 128 dims when LPP = 2 lanes share a position); output: lane owns dims
-    // [4 lane, 4 lane + 4) of both heads.
-    const int hq = lane >> 4, pl = (lane & 15) / LPP, hf = lane & (LPP - 1);
-    float m = -INFINITY, lsum = 0.f;          // running max / sum of this lane's head
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    // Tensor-core flash-decode (mma.sync m16n8k16 bf16, fp32 accumulation) over
+    // 16-position chunks, both GQA heads at once:
+    //   S[16 pos x 8] = K[16 x 128] * Qt, Q columns = q0 hi, q1 hi, q0 lo, q1 lo
+    //   (bf16 hi + lo parts of the fp32 q, so the scores carry ~16 bits of q);
+    //   Ot[128 dims x 8] += Vt * Pt, P columns the same hi/lo split of exp(s - m).
+    // K tiles come through ldmatrix, V tiles through ldmatrix.trans.
+    static_assert(ACH == 16, "tensor-core attention: 16-position chunks");
+    const int g = lane >> 2, t = lane & 3;
     const float scale = P.attn_scale;
-    const float4* qv = reinterpret_cast<const float4*>(q + hq * HD);
-    auto chunk = [&](const uint8_t* buf, int n) {
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(buf);
-        const uint16_t* vb = reinterpret_cast<const uint16_t*>(buf + ACH * HD * 2);
-        float sc = -INFINITY;
-        if (pl < n) {
-            const uint16_t* kr = kb + pl * HD;
-            float x0 = 0.f, x1 = 0.f;
-            constexpr int D4 = HD / 4 / LPP;   // 4-dim groups per lane
-#pragma unroll 8
-            for (int i = 0; i < D4; ++i) {
-                // rotated so that the lanes' rows (and halves) hit distinct banks
-                const int d4 = hf * D4 + ((i + pl + (D4 / 2) * hf) & (D4 - 1));
-                const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * d4);
-                const float4 qa = qv[d4];
-                x0 = fmaf(qa.x, bf16_bits_to_f32(kw.x & 0xffffu), x0);
-                x1 = fmaf(qa.y, bf16_bits_to_f32(kw.x >> 16), x1);
-                x0 = fmaf(qa.z, bf16_bits_to_f32(kw.y & 0xffffu), x0);
-                x1 = fmaf(qa.w, bf16_bits_to_f32(kw.y >> 16), x1);
-            }
-            sc = x0 + x1;
+    uint32_t qb[HD / 16][2];
+#pragma unroll
+    for (int k8 = 0; k8 < HD / 16; ++k8)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int d = 16 * k8 + 8 * hf + 2 * t;
+            qb[k8][hf] = g < 4 ? bf2_part(q[(g & 1) * HD + d], q[(g & 1) * HD + d + 1], g >> 1) : 0u;
         }
-        if (LPP == 2) sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-        sc = pl < n ? sc * scale : -INFINITY;
-        float mx = sc;
+    float acc[HD / 16][4];
 #pragma unroll
-        for (int o = 8; o >= LPP; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float nm = fmaxf(m, mx);
-        const float cf = expf(m - nm);
-        const float e = pl < n ? expf(sc - nm) : 0.f;
-        float es = e;
+    for (int mt = 0; mt < HD / 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;   // running max / sum of heads 0 and 1
+    // A chunk buffer holds K then V, each as two 16-row x 128-byte boxes (dims 0..63, 64..127) in the TMA
+    // 128-byte swizzle: 16-byte unit u of row r sits at unit u ^ (r & 7).
+    auto chunk = [&](uint8_t* buf, int n) {
+        const uint32_t kbase = smem_u32(buf), vbase = kbase + ACH * HD * 2;
+        if (n < ACH) {   // V rows past n must be finite (P is 0 there, and 0 * NaN would poison the sums)
+            uint4* zv = reinterpret_cast<uint4*>(buf + ACH * HD * 2);
+            for (int i = lane; i < 2 * (ACH - n) * 8; i += 32) {
+                const int bx = i / ((ACH - n) * 8), r = n + (i / 8) % (ACH - n);
+                zv[bx * ACH * 8 + r * 8 + (i & 7)] = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        const int sw = lane & 7;   // = row & 7 for the rows this lane addresses
+        const uint32_t ka = kbase + ((lane & 7) + ((lane >> 3) & 1) * 8) * 128;
 #pragma unroll
-        for (int o = 8; o >= LPP; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
-        lsum = lsum * cf + es;
-        m = nm;
-        const float c0 = __shfl_sync(0xffffffffu, cf, 0), c1 = __shfl_sync(0xffffffffu, cf, 16);
+        for (int k8 = 0; k8 < HD / 16; ++k8) {
+            uint32_t a[4];
+            ldsm_x4(a, ka + (k8 >> 2) * (ACH * 128) + ((((2 * k8 + (lane >> 4)) & 7) ^ sw) << 4));
+            mma16816(c, a, qb[k8][0], qb[k8][1]);
+        }
+        // hi + lo columns: lanes t = 0 hold (q0 hi, q1 hi), t = 1 (q0 lo, q1 lo)
+        float s0 = c[0] + __shfl_xor_sync(0xffffffffu, c[0], 1);   // position g, head 0
+        float s1 = c[1] + __shfl_xor_sync(0xffffffffu, c[1], 1);   // position g, head 1
+        float s2 = c[2] + __shfl_xor_sync(0xffffffffu, c[2], 1);   // position g + 8, head 0
+        float s3 = c[3] + __shfl_xor_sync(0xffffffffu, c[3], 1);   // position g + 8, head 1
+        const bool v0 = g < n, v1 = g + 8 < n;
+        s0 = v0 ? s0 * scale : -INFINITY; s1 = v0 ? s1 * scale : -INFINITY;
+        s2 = v1 ? s2 * scale : -INFINITY; s3 = v1 ? s3 * scale : -INFINITY;
+        float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
-        auto pv = [&](int p) {
-            const float ep0 = __shfl_sync(0xffffffffu, e, p * LPP), ep1 = __shfl_sync(0xffffffffu, e, 16 + p * LPP);
-            const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * lane);
-            const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
-            const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
-            a0[0] = fmaf(ep0, v0, a0[0]); a0[1] = fmaf(ep0, v1, a0[1]); a0[2] = fmaf(ep0, v2, a0[2]); a0[3] = fmaf(ep0, v3, a0[3]);
-            a1[0] = fmaf(ep1, v0, a1[0]); a1[1] = fmaf(ep1, v1, a1[1]); a1[2] = fmaf(ep1, v2, a1[2]); a1[3] = fmaf(ep1, v3, a1[3]);
-        };
-        if (n == ACH) {   // full chunk: unrolled, so the shuffles and loads of all positions overlap
+        for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        mx0 = __shfl_sync(0xffffffffu, mx0, 0);   // lanes t = 0 reduced the real scores
+        mx1 = __shfl_sync(0xffffffffu, mx1, 0);
+        const float n0 = fmaxf(mA, mx0), n1 = fmaxf(mB, mx1);
+        const float cf0 = expf(mA - n0), cf1 = expf(mB - n1);   // 0 while m is still -inf
+        const float e0 = v0 ? expf(s0 - n0) : 0.f, e1 = v0 ? expf(s1 - n1) : 0.f;
+        const float e2 = v1 ? expf(s2 - n0) : 0.f, e3 = v1 ? expf(s3 - n1) : 0.f;
+        float es0 = e0 + e2, es1 = e1 + e3;
 #pragma unroll
-            for (int p = 0; p < ACH; ++p) pv(p);
-        } else {
-            for (int p = 0; p < n; ++p) pv(p);
+        for (int o = 4; o < 32; o <<= 1) {
+            es0 += __shfl_xor_sync(0xffffffffu, es0, o);
+            es1 += __shfl_xor_sync(0xffffffffu, es1, o);
+        }
+        lA = lA * cf0 + __shfl_sync(0xffffffffu, es0, 0);
+        lB = lB * cf1 + __shfl_sync(0xffffffffu, es1, 0);
+        mA = n0;
+        mB = n1;
+#pragma unroll
+        for (int mt = 0; mt < HD / 16; ++mt) { acc[mt][0] *= cf0; acc[mt][1] *= cf1; acc[mt][2] *= cf0; acc[mt][3] *= cf1; }
+        // Pt fragment of column g (< 4: head g & 1, hi/lo part g >> 1): positions 2t, 2t + 1, 2t + 8, 2t + 9,
+        // held by lanes 4 * (2t) and 4 * (2t + 1)
+        const float a0_ = __shfl_sync(0xffffffffu, e0, 8 * t), a1_ = __shfl_sync(0xffffffffu, e1, 8 * t);
+        const float a2_ = __shfl_sync(0xffffffffu, e2, 8 * t), a3_ = __shfl_sync(0xffffffffu, e3, 8 * t);
+        const float b0_ = __shfl_sync(0xffffffffu, e0, 8 * t + 4), b1_ = __shfl_sync(0xffffffffu, e1, 8 * t + 4);
+        const float b2_ = __shfl_sync(0xffffffffu, e2, 8 * t + 4), b3_ = __shfl_sync(0xffffffffu, e3, 8 * t + 4);
+        const bool h1 = g & 1;
+        uint32_t pb0 = 0u, pb1 = 0u;
+        if (g < 4) {
+            pb0 = bf2_part(h1 ? a1_ : a0_, h1 ? b1_ : b0_, g >> 1);
+            pb1 = bf2_part(h1 ? a3_ : a2_, h1 ? b3_ : b2_, g >> 1);
+        }
+        const uint32_t va = vbase + ((lane & 7) + (lane >> 4) * 8) * 128;
+#pragma unroll
+        for (int mt = 0; mt < HD / 16; ++mt) {
+            uint32_t a[4];
+            ldsm_x4_t(a, va + (mt >> 2) * (ACH * 128) + ((((2 * mt + ((lane >> 3) & 1)) & 7) ^ sw) << 4));
+            mma16816(acc[mt], a, pb0, pb1);
         }
     };
     // cached positions [p0, p1) in ACH-position chunks, NBUF in flight per warp
-    const size_t head = (((size_t)cb * P.L + l) * NKVH + kvh) * (size_t)P.max_seq * HD;
+    const int head = ((cb * P.L + l) * NKVH + kvh) * P.max_seq;   // first tensor row of this (sequence, layer, head)
     const int nch = (p1 - p0 + ACH - 1) / ACH;
     auto issue = [&](int ci) {   // lane 0
-        const int p = p0 + ACH * ci, n = min(ACH, p1 - p);
+        const int row = head + p0 + ACH * ci;   // a whole box is copied; rows past the range are masked
         const int bi = ci % NBUF;
         uint8_t* buf = sm->a.kv[warp][bi];
+        uint64_t* bar = &sm->abar[warp][bi];
         fence_proxy_async();
-        mbar_arrive_expect_tx(&sm->abar[warp][bi], 2u * n * HD * 2);
-        bulk_g2s(buf, P.kc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][bi]);
-        bulk_g2s(buf + ACH * HD * 2, P.vc + head + (size_t)p * HD, n * HD * 2, &sm->abar[warp][bi]);
+        mbar_arrive_expect_tx(bar, 2u * ACH * HD * 2);
+        tma_load_2d(buf, &P.tm_k, 0, row, bar);
+        tma_load_2d(buf + ACH * 128, &P.tm_k, 64, row, bar);
+        tma_load_2d(buf + ACH * HD * 2, &P.tm_v, 0, row, bar);
+        tma_load_2d(buf + ACH * HD * 2 + ACH * 128, &P.tm_v, 64, row, bar);
     };
     __syncwarp();
     for (int ci = 0; ci < min(NBUF, nch); ++ci) {
@@ -792,19 +860,32 @@ __device__ void attn_item(Ctx& c, const Params& P, int l, int b, int kvh, int pa
         }
     }
     if (owner) {  // the current position from registers (all buffers are free now)
+        // row 0 of a box is unswizzled: dim i sits at box i / 64, byte 2 (i % 64)
         uint16_t* kw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0]);
         uint16_t* vw = reinterpret_cast<uint16_t*>(sm->a.kv[warp][0] + ACH * HD * 2);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { kw[lane + 32 * j] = kcur[j]; vw[lane + 32 * j] = vcur[j]; }
+        for (int j = 0; j < 4; ++j) {
+            const int i = lane + 32 * j, o = (i >> 6) * (ACH * 64) + (i & 63);
+            kw[o] = kcur[j];
+            vw[o] = vcur[j];
+        }
         __syncwarp();
         chunk(sm->a.kv[warp][0], 1);
     }
-    const float m0 = __shfl_sync(0xffffffffu, m, 0), m1 = __shfl_sync(0xffffffffu, m, 16);
-    const float l0 = __shfl_sync(0xffffffffu, lsum, 0), l1 = __shfl_sync(0xffffffffu, lsum, 16);
     float* out = P.part + (((size_t)b * NKVH + kvh) * MAX_SPLITS_B + s) * PARTW;
-    *reinterpret_cast<float4*>(out + 4 * lane) = make_float4(a0[0], a0[1], a0[2], a0[3]);
-    *reinterpret_cast<float4*>(out + HD + 4 * lane) = make_float4(a1[0], a1[1], a1[2], a1[3]);
-    if (lane == 0) { out[2 * HD] = m0; out[2 * HD + 1] = m1; out[2 * HD + 2] = l0; out[2 * HD + 3] = l1; }
+#pragma unroll
+    for (int mt = 0; mt < HD / 16; ++mt) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = acc[mt][j] + __shfl_xor_sync(0xffffffffu, acc[mt][j], 1);   // hi + lo
+        if (t == 0) {
+            out[16 * mt + g] = o[0];
+            out[HD + 16 * mt + g] = o[1];
+            out[16 * mt + g + 8] = o[2];
+            out[HD + 16 * mt + g + 8] = o[3];
+        }
+    }
+    if (lane == 0) { out[2 * HD] = mA; out[2 * HD + 1] = mB; out[2 * HD + 2] = lA; out[2 * HD + 3] = lB; }
 }
 
 
@@ -851,9 +932,10 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 // ---------------------------------------------------------------------------
 // The step kernel
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT, 1) batch_kernel(const Params P) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    Smem* sm = reinterpret_cast<Smem*>(smem_raw);
+__global__ void __launch_bounds__(NT, 1) batch_kernel(const __grid_constant__ Params P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the 128-byte-swizzled TMA boxes need 1024-byte aligned destinations: one spare KB is allocated
+    Smem* sm = reinterpret_cast<Smem*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
     Ctx c;
     init_ctx(c, sm, P.ctl, P.budget_ns);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1147,7 +1229,7 @@ __global__ void xpack_kernel(const float* x, uint8_t* xa, int K, int B, unsigned
 }
 
 __global__ void __launch_bounds__(NT, 1) matmul_kernel(const MMParams Q) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem* sm = reinterpret_cast<Smem*>(smem_raw);
     Ctx c;
     init_ctx(c, sm, Q.ctl, Q.budget_ns);
@@ -1241,7 +1323,7 @@ cudaError_t setup_device(int& dev) {
     if (dev < 0 || dev >= MAX_DEV) return cudaErrorInvalidDevice;
     if (!g_attr[dev]) {
         if ((e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-        if ((e = cudaFuncSetAttribute(batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem))) !=
+        if ((e = cudaFuncSetAttribute(batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem) + 1024)) !=
             cudaSuccess)
             return e;
         if ((e = cudaFuncSetAttribute(matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem))) !=
@@ -1250,6 +1332,28 @@ cudaError_t setup_device(int& dev) {
         g_attr[dev] = true;
     }
     return cudaSuccess;
+}
+
+// Tensor map of one KV cache as [rows][128] bf16 with 16 x 64 boxes in the 128-byte swizzle.  The
+// driver's encoder is fetched through the runtime, so the library does not link libcuda.
+cudaError_t encode_cache_map(CUtensorMap* map, const void* base, int rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)ACH};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 }  // namespace
 }  // namespace batch
@@ -1389,9 +1493,14 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
         P.lm_tiles = split_lo(VOCAB / TROWS, a->vocab_shards, a->vocab_shard + 1) - P.lm_tile0;
     }
     if (P.prefill && num_steps != 1) return MQ_ERR_ARG;
+    {
+        const int cache_rows = (a->prefill ? 1 : a->batch) * a->num_layers * NKVH * a->max_seq_len;
+        if ((e = encode_cache_map(&P.tm_k, a->k_cache, cache_rows)) != cudaSuccess) return (int)e;
+        if ((e = encode_cache_map(&P.tm_v, a->v_cache, cache_rows)) != cudaSuccess) return (int)e;
+    }
     void* args[] = {&P};
     for (int j = 0; j < num_steps; ++j) {
-        e = cudaLaunchCooperativeKernel((const void*)batch_kernel, dim3(g_sms[dev]), dim3(NT), args, sizeof(Smem), stream);
+        e = cudaLaunchCooperativeKernel((const void*)batch_kernel, dim3(g_sms[dev]), dim3(NT), args, sizeof(Smem) + 1024, stream);
         if (e != cudaSuccess) return (int)e;
     }
     return 0;

@@ -181,7 +181,10 @@ int mq_decode_multi(
  *     gate rows 16p..16p+15, tile 2p+1 = the same up rows; 6144 x 1024) packed
  *     with block_k 256; k/v/up pointers unused; the LM head packed with
  *     block_k 64; scales (ScalePointers, unchanged) fp32, norms and embedding bf16;
- *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128];
+ *   - k_cache / v_cache: bf16 [batch][num_layers][8][max_seq_len][128]
+ *     (batch * num_layers * 8 * max_seq_len below 2^31 rows, else MQ_ERR_SIZE:
+ *     the kernel reads them through 2-D TMA tensor maps with 32-bit row
+ *     coordinates);
  *   - tokens: device int32 [batch]: read as this step's inputs, overwritten
  *     with the argmax outputs (so repeated steps feed back on the device);
  *   - positions: device int32 [batch]: position of each sequence's input token

@@ -1494,7 +1494,10 @@ extern "C" int mq_batch_decode(const MQBatchArgs* a, int num_steps, cudaStream_t
     }
     if (P.prefill && num_steps != 1) return MQ_ERR_ARG;
     {
-        const int cache_rows = (a->prefill ? 1 : a->batch) * a->num_layers * NKVH * a->max_seq_len;
+        // the tensor maps and the kernel's row index address cache rows with 32-bit integers
+        const long long rows_ll = (long long)(a->prefill ? 1 : a->batch) * a->num_layers * NKVH * a->max_seq_len;
+        if (rows_ll + ACH > 0x7fffffffLL) return MQ_ERR_SIZE;
+        const int cache_rows = (int)rows_ll;
         if ((e = encode_cache_map(&P.tm_k, a->k_cache, cache_rows)) != cudaSuccess) return (int)e;
         if ((e = encode_cache_map(&P.tm_v, a->v_cache, cache_rows)) != cudaSuccess) return (int)e;
     }

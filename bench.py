@@ -334,7 +334,8 @@ def main():
     ap.add_argument("--ref-sample-steps", type=int, default=3)
     ap.add_argument("--ncu-case", action="store_true",
                     help="profiling case: 100 untimed steps, then 2 steps (capture with ncu -s 100 -c 1)")
-    ap.add_argument("--trace", action="store_true", help="print the per-phase timeline of one step at position 100")
+    ap.add_argument("--trace", action="store_true", help="print the per-phase timeline of one step at each --trace-pos")
+    ap.add_argument("--trace-pos", default="100", help="comma-separated positions for --trace")
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
                     help="BASELINE config: 1 INT8 (default, the headline), 2 BF16 weights, 3 long context, "
                          "4 batched (64 sequences per GPU)")
@@ -376,13 +377,25 @@ def main():
         if dist:
             dist.destroy_process_group()
         return
-    if args.ncu_case or args.trace:
+    if args.trace:
+        from megaqwen_b200 import trace
+        dec = build_decoder(args.layers, 256)
+        for p in (int(x) for x in args.trace_pos.split(",")):
+            dec.reset()
+            if p:
+                dec.decode_steps(5, p)
+            torch.cuda.synchronize()
+            out = trace.summarize(trace.capture_step(dec), args.layers)
+            out["position"] = p
+            print(json.dumps(out), flush=True)
+        dec.check_device()
+        return
+    if args.ncu_case:
         dec = build_decoder(args.layers, 256)
         dec.decode_steps(5, 100)
         torch.cuda.synchronize()
-        if args.trace:
-            from megaqwen_b200 import trace
-            print(json.dumps(trace.summarize(trace.capture_step(dec), args.layers)))
+        if False:
+            pass
         else:
             dec.decode_steps(5, 2)
             torch.cuda.synchronize()

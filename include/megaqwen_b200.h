@@ -111,13 +111,24 @@ int launch_a10_int8_decode(
  *     splits per KV head, which covers every position < max_seq_len.
  *   - The first call on a device does a one-time set-up (it looks up the
  *     device address of the static array and sets the kernel's shared-memory
- *     attribute); make that first call before any stream capture.
+ *     attribute); make that first call before any stream capture.  Under CUDA's
+ *     default lazy module loading that first call is also when the driver loads
+ *     the library's device code and places the static array in device memory:
+ *     callers whose arena claims the rest of device memory should make it during
+ *     their set-up (or run with CUDA_MODULE_LOADING=EAGER).
  *   - All calls on a device share the one array, which keeps the previous
  *     call's contents (the call clears the error word itself).  Calls that
  *     overlap on the GPU -- e.g. issued on two streams without ordering --
  *     race on it: serialise them.
- *   - A device-side failure (a bounded wait that ran out) is reported by
- *     *output_token_id == -1.
+ *   - A device-side failure (a bounded wait that ran out) is reported only by
+ *     *output_token_id == -1; the MQ_DEV_* code is not available on this path
+ *     (mq_device_status reads the allocating path's workspace and allocates it
+ *     on first use: do not call it here).  The next call starts clean.
+ *   - The hand-off tags are 32-bit epochs advanced by (num_layers + 1) * 8 per
+ *     call; the host clears the array before they wrap, counting the calls it
+ *     issues.  Replays of a captured graph holding this call are not counted:
+ *     keep them below 0xF0000000 / ((num_layers + 1) * 8) (about 13 million
+ *     for 28 layers) between direct calls.
  */
 int launch_a10_int8_decode_static(
     int input_token_id, int* output_token_id,
@@ -318,6 +329,13 @@ int mq_set_trace(unsigned long long* dev_buf, int slots_per_cta);
 
 /* Number of CTAs (one per SM) and dynamic shared memory the decode kernel uses. */
 int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads);
+
+/* Diagnostics of the current device (no reference counterpart):
+ * binary_version: the decode kernel's cudaFuncAttributes::binaryVersion
+ *   (100 = built for sm_100a and loaded as such);
+ * workspace_allocated: 1 if the allocating entry points have created their
+ *   per-device workspace on this device, else 0.  Allocates nothing. */
+int mq_library_info(int* binary_version, int* workspace_allocated);
 
 #ifdef __cplusplus
 }

@@ -28,35 +28,6 @@
 #define MQ_PHASE __device__ __forceinline__
 #endif
 
-// MQ_DEBUG_STAMPS (development aid, off by default): consumer thread 0 of CTA 1
-// appends (id, clock64) pairs to a buffer set with mqdbg_set_stamp_buffer.
-// MQ_NO_STREAM (timing experiment only, wrong results): no weight streaming.
-#ifndef MQ_NO_STREAM
-#define MQ_NO_STREAM 0
-#endif
-#ifndef MQ_DEBUG_STAMPS
-#define MQ_DEBUG_STAMPS 0
-#endif
-namespace mq {
-__device__ int g_dbg_n;
-__device__ unsigned long long* g_dbg_buf;
-__device__ __forceinline__ void dbg(int id) {
-#if MQ_DEBUG_STAMPS
-    __shared__ int s_n;  // set to 0 by dbg(-1) at kernel start
-    if (blockIdx.x == 1 && threadIdx.x == 0) {
-        const long long t = clock64();
-        if (id < 0) { s_n = 0; return; }
-        if (g_dbg_buf && s_n < 4000) {
-            g_dbg_buf[2 * s_n] = id;
-            g_dbg_buf[2 * s_n + 1] = t;
-            ++s_n;
-        }
-    }
-#else
-    (void)id;
-#endif
-}
-}  // namespace mq
 
 namespace mq {
 
@@ -129,7 +100,7 @@ __device__ __forceinline__ bool consumers_sync_abort(Ctx& c) {
         : "memory");
     return any != 0;
 }
-__device__ __forceinline__ void consumers_sync() { dbg(600); named_bar(1, NCT); dbg(700); }
+__device__ __forceinline__ void consumers_sync() { named_bar(1, NCT); }
 
 // ---------------------------------------------------------------------------
 // Work geometry, shared by producer and consumers so both walk the same chunks.
@@ -300,12 +271,7 @@ struct Cons {
 
     __device__ const uint8_t* wait(Ctx& c, int where) {
         const uint32_t stage = seq % NSTAGE;
-        dbg(100 + where);
-#if MQ_NO_STREAM
-        return sm->ring[stage];
-#endif
         mbar_wait(c, &sm->full[stage], (seq / NSTAGE) & 1, where);
-        dbg(200 + where);
         return sm->ring[stage];
     }
     __device__ void release() {
@@ -403,7 +369,6 @@ MQ_PHASE void mv_phase(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl s
             }
             const float dot = warp_sum(part);
             if (cs.lane == 0) out(r0 + i, dot * sc);
-            dbg(300);
         }
         cs.release();
     }
@@ -601,7 +566,6 @@ MQ_PHASE void rmsnorm_1024(Cons& cs, const float* src, const NormW& w, float* ds
 template <int MAXK, class Addr, class Store>
 __device__ __forceinline__ void poll_gather(Ctx& c, const Cons& cs, Addr addr, int n, uint32_t tag, int where,
                                             Store store) {
-    dbg(400 + where);
     uint64_t v[MAXK];
 #pragma unroll
     for (int k = 0; k < MAXK; ++k) {
@@ -630,7 +594,6 @@ __device__ __forceinline__ void poll_gather(Ctx& c, const Cons& cs, Addr addr, i
         const int i = cs.tid + k * NCT;
         if (i < n) store(i, (uint32_t)v[k]);
     }
-    dbg(500 + where);
 }
 
 template <int MAXK, class Store>
@@ -916,7 +879,6 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
     Workspace* ws = c.ws;
     const bool cta0 = G.b == 0;
-    dbg(-1);
     stage_pointers(P, cs, WT::HAS_SCALE);
     consumers_sync();
     if (WT::HAS_SCALE) stage_scales(P, cs, G);
@@ -1081,9 +1043,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
     __syncthreads();
     unsigned long long cta_key = 0ull;
     if (threadIdx.x >= NCT) {
-#if !MQ_NO_STREAM
         if (threadIdx.x == NCT) producer_main<WT>(P, c, G);
-#endif
     } else {
         consumer_main<WT>(P, c, G, epoch, token, cta_key);
     }
@@ -1162,7 +1122,7 @@ struct DevState {
     Workspace* ws = nullptr;
     int num_sms = 0;
     bool attr_set[4] = {false, false, false, false};
-    unsigned long long launches = 0;
+    unsigned long long epoch_used = 0;   // sum of the epoch increments of the launches since the last clear
 };
 DevState g_dev[MAX_DEV];
 unsigned long long g_budget_ns = 2000000000ull;
@@ -1227,14 +1187,16 @@ int launch_step(int kind, DecodeParams& P, cudaStream_t stream) {
     P.trace_slots = g_trace_slots;
     g_skip_cta = -1;
     P.splits = choose_splits(P.position + 1, d->num_sms);
-    // Tags are 32-bit epochs; clear the hand-off buffers long before they wrap.
+    // Tags are 32-bit epochs; every launch advances the device epoch by
+    // (L + 1) * TAGS_PER_LAYER.  Clear the hand-off buffers (and the epoch) long
+    // before it could wrap.  `epoch_used` sums the increments actually issued.
     const unsigned long long per_launch = (unsigned long long)(P.L + 1) * TAGS_PER_LAYER;
-    if ((d->launches + 1) * per_launch > 0xF0000000ull) {
+    if (d->epoch_used + per_launch > 0xF0000000ull) {
         cudaError_t e = cudaMemsetAsync(d->ws, 0, sizeof(Workspace), stream);
         if (e != cudaSuccess) return (int)e;
-        d->launches = 0;
+        d->epoch_used = 0;
     }
-    d->launches++;
+    d->epoch_used += per_launch;
     void* args[] = {&P};
     cudaError_t e;
     if (kind == 0) {
@@ -1418,19 +1380,23 @@ extern "C" int mq_kernel_info(int* num_ctas, int* smem_bytes, int* threads) {
     return (int)e;
 }
 
+extern "C" int mq_library_info(int* binary_version, int* workspace_allocated) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= MAX_DEV) return MQ_ERR_DEVICE;
+    cudaFuncAttributes a{};
+    if ((e = cudaFuncGetAttributes(&a, decode_kernel<W8>)) != cudaSuccess) return (int)e;
+    if (binary_version) *binary_version = a.binaryVersion;
+    if (workspace_allocated) *workspace_allocated = g_dev[dev].ws != nullptr ? 1 : 0;
+    return 0;
+}
+
 extern "C" int mq_set_trace(unsigned long long* dev_buf, int slots_per_cta) {
     if (dev_buf && slots_per_cta <= 0) return MQ_ERR_ARG;
     g_trace = dev_buf;
     g_trace_slots = dev_buf ? slots_per_cta : 0;
     return 0;
-}
-
-// Development aid, not part of the public header: stamp buffer of MQ_DEBUG_STAMPS builds.
-extern "C" int mqdbg_set_stamp_buffer(unsigned long long* buf) {
-    int zero = 0;
-    cudaError_t e = cudaMemcpyToSymbol(g_dbg_buf, &buf, sizeof(buf));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_dbg_n, &zero, sizeof(zero));
-    return (int)e;
 }
 
 // ===========================================================================
@@ -1456,7 +1422,7 @@ struct StaticDevState {
     mq::Workspace* ws = nullptr;   // device address of g_static_workspace on this device
     int num_sms = 0;
     bool attr_set = false;
-    unsigned long long launches = 0;
+    unsigned long long epoch_used = 0;   // sum of the epoch increments of the launches since the last clear
 };
 StaticDevState g_static_dev[mq::MAX_DEV_STATIC];
 }  // namespace
@@ -1499,12 +1465,12 @@ extern "C" int launch_a10_int8_decode_static(
     // argmax slot are self-resetting; the error word must start at zero, and
     // the tagged buffers are cleared before their 32-bit epochs could wrap.
     const unsigned long long per_launch = (unsigned long long)(num_layers + 1) * TAGS_PER_LAYER;
-    if ((d.launches + 1) * per_launch > 0xF0000000ull) {
+    if (d.epoch_used + per_launch > 0xF0000000ull) {
         if ((e = cudaMemsetAsync(d.ws, 0, sizeof(Workspace), stream)) != cudaSuccess) return (int)e;
-        d.launches = 0;
+        d.epoch_used = 0;
     }
     if ((e = cudaMemsetAsync(&d.ws->err_code, 0, 2 * sizeof(int), stream)) != cudaSuccess) return (int)e;
-    d.launches++;
+    d.epoch_used += per_launch;
     DecodeParams P{};
     P.embed = embed_weight; P.layers = layer_weights; P.scales = scales; P.final_norm = final_norm_weight;
     P.lm_w = lm_head_weight; P.lm_scale = lm_head_scale;
@@ -1515,7 +1481,8 @@ extern "C" int launch_a10_int8_decode_static(
     P.attn_scale = attn_scale;
     P.ws = d.ws;
     P.budget_ns = g_budget_ns;
-    P.skip_cta = -1;
+    P.skip_cta = g_skip_cta;   // test hook (mq_inject_skip_publish), one call only
+    g_skip_cta = -1;
     P.splits = choose_splits(position + 1, d.num_sms);
     void* args[] = {&P};
     return (int)cudaLaunchCooperativeKernel((const void*)decode_kernel<W8>, dim3(d.num_sms), dim3(NTHREADS), args,

@@ -6,7 +6,9 @@
 //   scale  = fp32(bf16(absmax / 127))  (torch divides a bf16 tensor by a python
 //            scalar in fp32 and rounds the quotient to bf16; fp32 division and
 //            multiplication by fp32(1/127) give the same bf16 for every finite
-//            bf16 input, which tests/test_quant.py checks exhaustively)
+//            bf16 input, which
+//            tests/test_oracle_golden.py::test_scale_division_unambiguous_for_all_bf16
+//            checks exhaustively)
 //   scale  = max(scale, 1e-12)
 //   q      = clamp(rint(fp32(W) / scale), -128, 127)  (IEEE division, round half even)
 // This file is compiled without --use_fast_math and uses __fdiv_rn explicitly.

@@ -26,6 +26,7 @@ EXPORTED = (
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
     "mq_set_trace", "launch_a10_int8_decode_static", "mq_batch_workspace_bytes", "mq_batch_decode",
     "mq_batch_status", "mq_pack_weight_tiles", "mq_pack_weight_slabs", "mq_batch_matmul_workspace_bytes", "mq_batch_matmul",
+    "mq_library_info",
 )
 
 
@@ -78,6 +79,7 @@ def load():
     lib.mq_batch_matmul.argtypes = [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, ctypes.c_size_t, _vp]
     lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]
     lib.mq_kernel_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
+    lib.mq_library_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i)]
     for name in EXPORTED:
         getattr(lib, name).restype = _i
     _lib = lib
@@ -111,6 +113,13 @@ def set_wait_budget_ns(ns):
 
 def inject_skip_publish(enable, cta=0):
     check(load().mq_inject_skip_publish(1 if enable else 0, int(cta)), "mq_inject_skip_publish")
+
+
+def library_info():
+    """{"binary_version": decode kernel binaryVersion, "workspace_allocated": bool} on the current device."""
+    a, b = _i(0), _i(0)
+    check(load().mq_library_info(ctypes.byref(a), ctypes.byref(b)), "mq_library_info")
+    return {"binary_version": a.value, "workspace_allocated": bool(b.value)}
 
 
 def kernel_info():

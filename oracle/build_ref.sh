@@ -7,9 +7,10 @@
 #   libref_bf16.so : a10_decode_kernel.cu (includes config.cuh itself)
 # Flags follow bench_int8.py:262-263 / a10_decode.py:270-277 with the arch
 # changed to sm_100a.  Usage: oracle/build_ref.sh [reference_dir]
+# (default: $MQ_REFERENCE_DIR, else a directory named "reference" beside this repository)
 set -euo pipefail
-REF="${1:-${MQ_REFERENCE_DIR:-/root/reference}}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
+REF="${1:-${MQ_REFERENCE_DIR:-$(dirname "$(dirname "$HERE")")/reference}}"
 OUT="$HERE/_ref"
 [ -f "$REF/a10_int8_decode_kernel.cu" ] || { echo "reference not found at $REF" >&2; exit 1; }
 mkdir -p "$OUT"

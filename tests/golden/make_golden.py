@@ -1,7 +1,7 @@
 """Generate tests/golden/golden.pt by running the REFERENCE's own Python code.
 
-Run in a container that has the reference checkout (default /root/reference,
-or $MQ_REFERENCE_DIR):  python tests/golden/make_golden.py
+Run in a container that has the reference checkout ($MQ_REFERENCE_DIR, else a
+directory named "reference" beside this repository):  python tests/golden/make_golden.py
 The fixture is committed; the GPU box never needs the reference.
 
 What is recorded (all on the CPU, seeded):
@@ -25,9 +25,9 @@ import sys
 
 import torch
 
-REF = os.environ.get("MQ_REFERENCE_DIR", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("MQ_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
 sys.dont_write_bytecode = True
 sys.path.insert(0, os.path.join(ROOT, "megaqwen-a10_b200"))
 sys.path.insert(0, REF)

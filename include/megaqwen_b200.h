@@ -55,7 +55,8 @@ enum {
     MQ_ERR_TOKEN = -2,      /* token id outside [0, vocab) */
     MQ_ERR_POSITION = -3,   /* position outside [0, max_seq_len) or cache_len != position+1 */
     MQ_ERR_DEVICE = -4,     /* device has too few SMs / shared memory for the kernel */
-    MQ_ERR_SIZE = -5        /* a size is larger than the entry point supports */
+    MQ_ERR_SIZE = -5,       /* a size is larger than the entry point supports */
+    MQ_ERR_DEVICE_STEP = -6 /* mq_decode_step_host: the kernel reported a device-side error */
 };
 
 /* Device-side status codes written by the decode kernel (mq_device_status). */
@@ -178,6 +179,41 @@ int mq_decode_multi(
     void* k_cache, void* v_cache, float* g_normalized, float* d_logits, float* d_layer_hidden,
     int num_layers, int position, int max_seq_len, float attn_scale, int row_pad_bytes,
     cudaStream_t stream);
+
+/*
+ * Host-synchronous single step for the reference-facing decode_step(int) -> int
+ * (bench_int8.py:193-219: one launch, then .item()).  No reference counterpart
+ * as a C entry point: it exists so that the per-token host cost of that call is
+ * one short C call.  The caller fills an MQStepPlan once (all pointers of the
+ * decoder, which stay fixed) and passes only the token and position per step.
+ *   - host_token: a pinned host int32 (cudaHostAlloc / torch pin_memory), which
+ *     the kernel writes directly (mapped under unified addressing).
+ *   - launches one step on `stream`, synchronises the stream and returns the
+ *     token in *out_token; a device-side failure returns MQ_ERR_DEVICE_STEP
+ *     (mq_device_status then has the MQ_DEV_* code).
+ */
+typedef struct MQStepPlan {
+    int weight_kind;                 /* 0 = INT8, 1 = BF16 */
+    int num_layers;
+    int max_seq_len;
+    int row_pad_bytes;               /* 0 or 16, as for mq_decode_multi */
+    float attn_scale;
+    const void* embed_weight;
+    const LayerWeights* layer_weights;
+    const void* final_norm_weight;
+    const void* lm_head_weight;
+    const float* lm_head_scale;      /* INT8 only */
+    const ScalePointers* scales;     /* INT8 only */
+    const void* cos_table;
+    const void* sin_table;
+    void* k_cache;
+    void* v_cache;
+    float* g_normalized;             /* optional */
+    int* host_token;                 /* pinned host int32 */
+} MQStepPlan;
+
+int mq_decode_step_host(const MQStepPlan* plan, int input_token, int position, cudaStream_t stream,
+                        int* out_token);
 
 /*
  * Batched greedy decode (no reference counterpart: the

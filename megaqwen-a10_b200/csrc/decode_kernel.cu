@@ -1310,6 +1310,36 @@ extern "C" int mq_decode_multi(int weight_kind, int input_token, const int* d_to
     return 0;
 }
 
+extern "C" int mq_decode_step_host(const MQStepPlan* plan, int input_token, int position, cudaStream_t stream,
+                                   int* out_token) {
+    if (!plan || !out_token || !plan->host_token) return MQ_ERR_ARG;
+    const MQStepPlan& q = *plan;
+    if (q.weight_kind != 0 && q.weight_kind != 1) return MQ_ERR_ARG;
+    if (q.row_pad_bytes != 0 && q.row_pad_bytes != ROW_SKEW) return MQ_ERR_ARG;
+    if (input_token < 0 || input_token >= VOCAB) return MQ_ERR_TOKEN;
+    int rc = check_common(q.embed_weight, q.layer_weights, q.final_norm_weight, q.lm_head_weight, q.cos_table,
+                          q.sin_table, q.k_cache, q.v_cache, q.num_layers, position, q.max_seq_len);
+    if (rc) return rc;
+    if (q.weight_kind == 0 && (!q.lm_head_scale || !q.scales)) return MQ_ERR_ARG;
+    DecodeParams P{};
+    P.embed = q.embed_weight; P.layers = q.layer_weights; P.scales = q.scales; P.final_norm = q.final_norm_weight;
+    P.lm_w = q.lm_head_weight; P.lm_scale = q.lm_head_scale;
+    P.cos_t = (const __nv_bfloat16*)q.cos_table; P.sin_t = (const __nv_bfloat16*)q.sin_table;
+    P.kc = (__nv_bfloat16*)q.k_cache; P.vc = (__nv_bfloat16*)q.v_cache;
+    P.g_normalized = q.g_normalized;
+    P.token_out = q.host_token;     // pinned host memory, written by the kernel's last CTA
+    P.token_in = input_token; P.L = q.num_layers; P.position = position; P.max_seq = q.max_seq_len;
+    P.attn_scale = q.attn_scale; P.row_pad = q.row_pad_bytes;
+    *(volatile int*)q.host_token = -2;
+    if ((rc = launch_step(q.weight_kind, P, stream))) return rc;
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return (int)e;
+    const int t = *(volatile int*)q.host_token;
+    if (t < 0) return MQ_ERR_DEVICE_STEP;
+    *out_token = t;
+    return 0;
+}
+
 extern "C" int mq_matvec(int weight_kind, const void* W, const float* scale, const float* x, float* y, int M, int K,
                          cudaStream_t stream) {
     if (!W || !x || !y || M <= 0) return MQ_ERR_ARG;

@@ -16,6 +16,7 @@ MQ_ERRORS = {
     -3: "position outside [0, max_seq_len) or cache_len != position + 1",
     -4: "device unsupported",
     -5: "size larger than the entry point supports",
+    -6: "the kernel reported a device-side error",
 }
 ROW_PAD = 16  # padding bytes after every weight row in the layout the decoder classes use
 MQ_DEV_ERRORS = {1: "exchange wait timed out", 2: "weight-ring wait timed out", 3: "invalid token",
@@ -26,7 +27,7 @@ EXPORTED = (
     "mq_matvec", "mq_device_status", "mq_set_wait_budget_ns", "mq_inject_skip_publish", "mq_kernel_info",
     "mq_set_trace", "launch_a10_int8_decode_static", "mq_batch_workspace_bytes", "mq_batch_decode",
     "mq_batch_status", "mq_pack_weight_tiles", "mq_pack_weight_slabs", "mq_batch_matmul_workspace_bytes", "mq_batch_matmul",
-    "mq_library_info",
+    "mq_library_info", "mq_decode_step_host",
 )
 
 
@@ -42,6 +43,15 @@ class ScalePointers(ctypes.Structure):
     """Field order of config.cuh:59-67."""
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "q_scale", "k_scale", "v_scale", "o_scale", "gate_scale", "up_scale", "down_scale")]
+
+
+class MQStepPlan(ctypes.Structure):
+    """Field order of MQStepPlan (include/megaqwen_b200.h)."""
+    _fields_ = [("weight_kind", ctypes.c_int), ("num_layers", ctypes.c_int), ("max_seq_len", ctypes.c_int),
+                ("row_pad_bytes", ctypes.c_int), ("attn_scale", ctypes.c_float)] + \
+               [(n, ctypes.c_void_p) for n in (
+                   "embed_weight", "layer_weights", "final_norm_weight", "lm_head_weight", "lm_head_scale", "scales",
+                   "cos_table", "sin_table", "k_cache", "v_cache", "g_normalized", "host_token")]
 
 
 class MQError(RuntimeError):
@@ -80,6 +90,7 @@ def load():
     lib.launch_a10_int8_decode_static.argtypes = [_i] + [_vp] * 11 + [_i, _i, _i, _i, _f, _vp, _vp]
     lib.mq_kernel_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]
     lib.mq_library_info.argtypes = [ctypes.POINTER(_i), ctypes.POINTER(_i)]
+    lib.mq_decode_step_host.argtypes = [ctypes.POINTER(MQStepPlan), _i, _i, _vp, ctypes.POINTER(_i)]
     for name in EXPORTED:
         getattr(lib, name).restype = _i
     _lib = lib

@@ -118,20 +118,53 @@ class _MegakernelDecoderBase:
         host = torch.frombuffer(bytearray(bytes(carr)), dtype=torch.uint8)
         return host.to(self.device)
 
+    def _make_plan(self):
+        """The fixed launch arguments of decode_step, filled once (MQStepPlan)."""
+        scale_lm, scales = self._scale_ptrs()
+        self._host_token = torch.empty(1, dtype=torch.int32).pin_memory()
+        pl = _lib.MQStepPlan()
+        pl.weight_kind, pl.num_layers, pl.max_seq_len = self._kind, self.num_layers_, self.max_seq_len_
+        pl.row_pad_bytes, pl.attn_scale = _lib.ROW_PAD, self.attn_scale_
+        pl.embed_weight = self.embed_weight_.data_ptr()
+        pl.layer_weights = self.d_layer_weights_pad_.data_ptr()
+        pl.final_norm_weight = self.final_norm_weight_.data_ptr()
+        pl.lm_head_weight = self.lm_head_pad_.data_ptr()
+        pl.lm_head_scale, pl.scales = scale_lm.value, scales.value
+        pl.cos_table, pl.sin_table = self.cos_table_.data_ptr(), self.sin_table_.data_ptr()
+        pl.k_cache, pl.v_cache = self.k_cache_.data_ptr(), self.v_cache_.data_ptr()
+        pl.g_normalized = self.g_normalized_.data_ptr()
+        pl.host_token = self._host_token.data_ptr()
+        self._plan = pl
+        self._plan_ref = ctypes.byref(pl)
+        self._step_out = ctypes.c_int(0)
+        self._step_out_ref = ctypes.byref(self._step_out)
+        self._step_fn = _lib.load().mq_decode_step_host
+        self._dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+
     # -- reference methods -------------------------------------------------
     def decode_step(self, input_token_id):
-        """One greedy step at position(); returns the argmax token (syncs)."""
+        """One greedy step at position(); returns the argmax token (syncs).
+        One C call (mq_decode_step_host): launch on the current stream, the kernel
+        writes the token into pinned host memory, stream synchronise."""
         tok = int(input_token_id)
         if not 0 <= tok < VOCAB_SIZE:
             raise ValueError(f"token {tok} outside [0, {VOCAB_SIZE})")
         if self.position_ >= self.max_seq_len_:
             raise ValueError(f"KV cache full: position {self.position_} >= max_seq_len {self.max_seq_len_}")
-        self._run(tok, None, self.output_token_, 1, None, None)
-        out = int(self.output_token_.item())
-        if out < 0:
-            _lib.raise_device_error("decode_step")
-            raise _lib.MQError("decode_step: kernel reported no token")
-        return out
+        if getattr(self, "_plan", None) is None:
+            self._make_plan()
+        if torch.cuda.current_device() != self._dev_index:
+            with torch.cuda.device(self.device):
+                return self.decode_step(tok)
+        rc = self._step_fn(self._plan_ref, tok, self.position_, torch.cuda.current_stream().cuda_stream,
+                           self._step_out_ref)
+        if rc:
+            if rc == -6:
+                _lib.raise_device_error("decode_step")
+                raise _lib.MQError("decode_step: kernel reported no token")
+            _lib.check(rc, "mq_decode_step_host")
+        self.position_ += 1
+        return self._step_out.value
 
     def reset(self):
         self.position_ = 0

@@ -269,6 +269,7 @@ struct Cons {
     uint32_t seq;
     int warp, lane, tid;
 
+
     __device__ const uint8_t* wait(Ctx& c, int where) {
         const uint32_t stage = seq % NSTAGE;
         mbar_wait(c, &sm->full[stage], (seq / NSTAGE) & 1, where);
@@ -483,16 +484,16 @@ __device__ __forceinline__ float limb_finish(long long a0, long long a1, long lo
 // Streaming phase (LM head, stand-alone matvec): every ring chunk is one tile
 // (<= 16 rows) done by one warp (chunk q -> warp q % NCW) over all k-steps.
 // out(row, value) is called by lanes t == 0 (two rows each).
+// The limbs of the activation (scale 2^-k = inv) are already in shared memory
+// (sm->limb rows 0-2; row 3 all zero).
 template <int K, class Scl, class Out>
-__device__ __forceinline__ void mma_stream(Ctx& c, Cons& cs, int r0, int r1, const float* x_s, Scl scl, Out out) {
+__device__ __forceinline__ void mma_stream(Ctx& c, Cons& cs, int r0, int r1, float inv, Scl scl, Out out) {
     constexpr int RS = K + ROW_SKEW;
     constexpr int RPC = STAGE_BYTES / RS;
     constexpr int KS = K / 32;
     static_assert(RPC <= 16, "one tile per chunk");
-    build_limbs(cs, x_s, K);
     const int g = cs.lane >> 2, t = cs.lane & 3;
     const int* lb = cs.sm->limb[g < 3 ? g : 3];
-    const float inv = cs.sm->limb_inv;
     const int n = r1 - r0;
     for (int cb = 0, q = 0; cb < n; cb += RPC, ++q) {
         const uint8_t* st = cs.wait(c, 1);
@@ -520,44 +521,6 @@ __device__ __forceinline__ void mma_stream(Ctx& c, Cons& cs, int r0, int r1, con
         }
         cs.release();
     }
-}
-
-constexpr int NORM_PER = (HIDDEN + NCT - 1) / NCT;
-struct NormW {  // one thread's share of a 1024-wide bf16 norm weight, loaded ahead of use
-    float v[NORM_PER];
-    __device__ __forceinline__ void load(const Cons& cs, const void* w) {
-        const __nv_bfloat16* p = (const __nv_bfloat16*)w;
-#pragma unroll
-        for (int k = 0; k < NORM_PER; ++k) {
-            const int i = cs.tid + k * NCT;
-            v[k] = i < HIDDEN ? __bfloat162float(__ldg(p + i)) : 0.f;
-        }
-    }
-};
-
-// RMSNorm of src[1024] (fp32, smem) -> dst (smem) over the consumer threads:
-// x * rsqrt(mean(x^2) + eps) * w  (int8_decoder.py:228-232).  The weight is
-// already in registers (NormW), so no global load sits on the critical path.
-MQ_PHASE void rmsnorm_1024(Cons& cs, const float* src, const NormW& w, float* dst) {
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < NORM_PER; ++k) {
-        const int i = cs.tid + k * NCT;
-        if (i < HIDDEN) ss += src[i] * src[i];
-    }
-    ss = warp_sum(ss);
-    if (cs.lane == 0) cs.sm->red[cs.warp] = ss;
-    consumers_sync();
-    float tot = 0.f;
-#pragma unroll
-    for (int i = 0; i < NCW; ++i) tot += cs.sm->red[i];
-    const float rstd = rsqrtf(tot / (float)HIDDEN + RMS_EPS);
-#pragma unroll
-    for (int k = 0; k < NORM_PER; ++k) {
-        const int i = cs.tid + k * NCT;
-        if (i < HIDDEN) dst[i] = src[i] * rstd * w.v[k];
-    }
-    consumers_sync();
 }
 
 // Gather n tagged words addr(0..n) into the consumer threads: thread t owns
@@ -596,10 +559,272 @@ __device__ __forceinline__ void poll_gather(Ctx& c, const Cons& cs, Addr addr, i
     }
 }
 
-template <int MAXK, class Store>
-__device__ __forceinline__ void poll_block(Ctx& c, const Cons& cs, const uint64_t* base, int n, uint32_t tag,
-                                           int where, Store store) {
-    poll_gather<MAXK>(c, cs, [&](int i) { return base + i; }, n, tag, where, store);
+
+// ---------------------------------------------------------------------------
+// Exchange gather that leaves the next matvec's input ready.
+//
+// Thread t owns the groups of four consecutive words g = t, t + NCT, ... of an
+// n-word exchange.  It polls them with one 32-byte load per group and round
+// (the number of poll requests, not their size, sets the exchange latency:
+// 8-byte polls cost ~13 us per layer more than 32-byte ones), and forms v_i (the
+// payload as fp32) and y_i = v_i * w_i (w: the RMSNorm weight of the next
+// matvec, or 1).  y goes to xs (fp32, shared memory), v to keep when given.  One
+// consumer barrier reduces, in a fixed order, max|y| (the limb scale 2^k) and,
+// for a normalised input, sum(v^2) (rstd = rsqrt(mean + eps)); then every
+// thread splits its own y values into the three int8 limbs of y * 2^k and a
+// second barrier publishes them.  The norm's rstd is applied to the matvec
+// outputs: W (v * w * rstd) = rstd * W (v * w).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ld_relaxed_v4(const uint64_t* p, uint64_t (&v)[4]) {
+    asm volatile("ld.relaxed.gpu.global.v4.b64 {%0, %1, %2, %3}, [%4];"
+                 : "=l"(v[0]), "=l"(v[1]), "=l"(v[2]), "=l"(v[3]) : "l"(p) : "memory");
+}
+
+// Each 8-byte word of the vector access is single-copy atomic, so a word's tag
+// and payload arrive together.
+template <int MAXG>
+__device__ __forceinline__ void poll_groups(Ctx& c, const Cons& cs, const uint64_t* base, int ngroups, uint32_t tag,
+                                            int where, uint32_t (&pay)[MAXG][4]) {
+    uint64_t v[MAXG][4];
+#pragma unroll
+    for (int k = 0; k < MAXG; ++k) {
+        const int g = cs.tid + k * NCT;
+        if (g < ngroups) ld_relaxed_v4(base + 4 * g, v[k]);
+        else v[k][0] = v[k][1] = v[k][2] = v[k][3] = (uint64_t)tag << 32;
+    }
+    unsigned long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        bool done = true;
+#pragma unroll
+        for (int k = 0; k < MAXG; ++k) {
+            const int g = cs.tid + k * NCT;
+            if ((uint32_t)(v[k][0] >> 32) != tag || (uint32_t)(v[k][1] >> 32) != tag ||
+                (uint32_t)(v[k][2] >> 32) != tag || (uint32_t)(v[k][3] >> 32) != tag) {
+                done = false;
+                ld_relaxed_v4(base + 4 * g, v[k]);
+            }
+        }
+        if (done) break;
+        if ((it & 127) == 127) {
+            if (t0 == 0) t0 = globaltimer();
+            if (aborted(c)) break;
+            if (globaltimer() - t0 > c.budget) { record_error(c, MQ_DEV_TIMEOUT_EXCHANGE, where); break; }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < MAXG; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pay[k][e] = (uint32_t)v[k][e];
+}
+
+struct InputScale {
+    float inv;   // 2^-k of the limbs (1 without limbs)
+    float rstd;  // RMSNorm factor of a normalised input (1 otherwise)
+};
+
+// Norm weights of this thread's group (elements 4t .. 4t+3 of a 1024-wide
+// vector), loaded one phase ahead of use and kept as raw bf16 pairs: converting
+// at load time would make the thread wait for the load right there.
+struct NormW4 {
+    uint32_t raw[2];
+    __device__ __forceinline__ void load(const Cons& cs, const void* w) {
+        raw[0] = raw[1] = 0u;
+        if (cs.tid < HIDDEN / 4) {
+            const uint16_t* p = reinterpret_cast<const uint16_t*>(w) + 4 * cs.tid;
+            if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+                const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+                raw[0] = u.x; raw[1] = u.y;
+            } else {
+                raw[0] = (uint32_t)__ldg(p) | ((uint32_t)__ldg(p + 1) << 16);
+                raw[1] = (uint32_t)__ldg(p + 2) | ((uint32_t)__ldg(p + 3) << 16);
+            }
+        }
+    }
+    __device__ __forceinline__ float get(int e) const {
+        const uint32_t w = raw[e >> 1];
+        return bf16_bits_to_f32((e & 1) ? (w >> 16) : (w & 0xffffu));
+    }
+};
+
+// Second half of the gather: payloads (bf16 bits or fp32 bits) -> xs / keep /
+// limbs as described above.  NORM requires ngroups == HIDDEN / 4 (MAXG == 1).
+// LIMBS: two consumer barriers; otherwise one.
+template <int MAXG, bool LIMBS, bool NORM>
+MQ_PHASE InputScale finish_input(Cons& cs, const uint32_t (&pay)[MAXG][4], int ngroups, bool bf16pay,
+                                 const NormW4& w, float* xs, float* keep) {
+    static_assert(!NORM || MAXG == 1, "normalised inputs are 1024 wide");
+    Smem* sm = cs.sm;
+    float y[MAXG][4];
+    float mx = 0.f, ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < MAXG; ++k) {
+        const int g = cs.tid + k * NCT;
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[e] = bf16pay ? bf16_bits_to_f32(pay[k][e] & 0xffffu) : __uint_as_float(pay[k][e]);
+            if (g >= ngroups) v[e] = 0.f;
+            ss = fmaf(v[e], v[e], ss);
+            y[k][e] = NORM ? v[e] * w.get(e) : v[e];
+            mx = fmaxf(mx, fabsf(y[k][e]));
+        }
+        if (g < ngroups) {
+            *reinterpret_cast<float4*>(xs + 4 * g) = make_float4(y[k][0], y[k][1], y[k][2], y[k][3]);
+            if (keep) *reinterpret_cast<float4*>(keep + 4 * g) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+    }
+    if (LIMBS) mx = warp_max(mx);
+    if (NORM) ss = warp_sum(ss);
+    if (cs.lane == 0) { sm->red[cs.warp] = ss; sm->red2[cs.warp] = mx; }
+    consumers_sync();
+    InputScale out{1.f, 1.f};
+    if (NORM) {
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < NCW; ++i) tot += sm->red[i];
+        out.rstd = rsqrtf(tot / (float)HIDDEN + RMS_EPS);
+    }
+    if (LIMBS) {
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < NCW; ++i) m = fmaxf(m, sm->red2[i]);
+        float inv;
+        const float up = limb_scale(m, inv);
+        out.inv = inv;
+#pragma unroll
+        for (int k = 0; k < MAXG; ++k) {
+            const int g = cs.tid + k * NCT;
+            if (g < ngroups) {
+                uint32_t p0 = 0, p1 = 0, p2 = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) limb_split(y[k][e], up, p0, p1, p2, e);
+                sm->limb[0][g] = (int)p0; sm->limb[1][g] = (int)p1; sm->limb[2][g] = (int)p2;
+            }
+        }
+        consumers_sync();
+    }
+    return out;
+}
+
+// Row sums of R rows held per lane, reduced over the warp with R-way transposed
+// butterflies (R = 1, 2: 5 shuffles; R = 3, 4: 6).  Lane L ends with the full
+// sum of row L >> 4 (R = 2) or L >> 3 (R = 3, 4); any lane for R = 1.
+template <int R>
+__device__ __forceinline__ float xreduce(const float (&v)[R], int lane) {
+    if constexpr (R == 1) {
+        return warp_sum(v[0]);
+    } else if constexpr (R == 2) {
+        const bool hi = lane & 16;
+        float k = hi ? v[1] : v[0];
+        const float s = hi ? v[0] : v[1];
+        k += __shfl_xor_sync(0xffffffffu, s, 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
+        return k;
+    } else {
+        static_assert(R == 3 || R == 4, "");
+        const float v3 = R == 4 ? v[R - 1] : 0.f;
+        const bool hi = lane & 16;
+        float k0 = hi ? v[2] : v[0], k1 = hi ? v3 : v[1];
+        const float s0 = hi ? v[0] : v[2], s1 = hi ? v[1] : v3;
+        k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+        k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+        const bool h8 = lane & 8;
+        float k = h8 ? k1 : k0;
+        const float s = h8 ? k0 : k1;
+        k += __shfl_xor_sync(0xffffffffu, s, 8);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
+        return k;
+    }
+}
+// a2 * 2^16 + a1 * 2^8 + a0 in fp32 (a1 * 256 + a0 fits int32; one rounding in the fma).
+__device__ __forceinline__ float limb_sum_f32(int a0, int a1, int a2) {
+    return fmaf((float)a2, 65536.f, (float)(a1 * 256 + a0));
+}
+
+// INT8 matvec over rows [r0, r1) of one projection (K wide) on the limbs the
+// gather left in shared memory.  The phase's chunks (MAXCH at most) are taken
+// together; warp w handles rows w, w + NCW, ... (RMAX at most) at once, so the
+// loads and dp4a chains of its rows overlap and one transposed reduction ends
+// them.  out(row, dot * 2^-k * scl(row)) is called once per row.
+template <int K, int RMAX, int MAXCH, class Scl, class Out>
+MQ_PHASE void mv_rows8(Ctx& c, Cons& cs, int r0, int r1, float inv, Scl scl, Out out) {
+    constexpr int RS = K + ROW_SKEW;
+    constexpr int RPC = STAGE_BYTES / RS;
+    constexpr int UPL = K / 512;
+    const int n = r1 - r0;
+    const int nch = (n + RPC - 1) / RPC;
+    Limbs<UPL * 4> lb;
+    lb.load(cs.sm->limb[0], cs.sm->limb[1], cs.sm->limb[2], cs.lane, inv);
+    const uint8_t* st[MAXCH];
+#pragma unroll
+    for (int q = 0; q < MAXCH; ++q) st[q] = q < nch ? cs.wait_at(c, q, 1) : nullptr;
+    int acc[RMAX][3];
+    const uint4* rowp[RMAX];
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+        acc[r][0] = acc[r][1] = acc[r][2] = 0;
+        const int i = cs.warp + NCW * r;
+        rowp[r] = i < n ? reinterpret_cast<const uint4*>(pick(st, i / RPC) + (size_t)(i % RPC) * RS) : nullptr;
+    }
+#pragma unroll
+    for (int j = 0; j < UPL; ++j)
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r)
+            if (rowp[r]) lb.acc(rowp[r][cs.lane + 32 * j], j, acc[r][0], acc[r][1], acc[r][2]);
+    float v[RMAX];
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) v[r] = limb_sum_f32(acc[r][0], acc[r][1], acc[r][2]);
+    const float tot = xreduce<RMAX>(v, cs.lane);
+    const int rr = RMAX == 1 ? 0 : (RMAX == 2 ? cs.lane >> 4 : cs.lane >> 3);
+    const int lead = RMAX == 1 ? 0 : (RMAX == 2 ? (cs.lane & 15) : (cs.lane & 7));
+    const int i = cs.warp + NCW * rr;
+    if (lead == 0 && rr < RMAX && i < n) out(r0 + i, tot * inv * scl(r0 + i));
+    cs.release_n(nch);
+}
+
+// gate/up pairs [p0, p1) (INT8, limbs in shared memory): warp w handles pairs
+// w and w + NCW at once (4 rows); val(gate, up) -> published value.
+template <int MAXCH, class Val, class Out>
+MQ_PHASE void gu_rows8(Ctx& c, Cons& cs, int p0, int p1, float inv, const float* sg, const float* su, Val val,
+                       Out out) {
+    constexpr int K = HIDDEN;
+    constexpr int RS = K + ROW_SKEW;
+    constexpr int PPC = STAGE_BYTES / (2 * RS);   // pairs per chunk
+    constexpr int UPL = K / 512;
+    const int n = p1 - p0;
+    const int nch = (n + PPC - 1) / PPC;
+    Limbs<UPL * 4> lb;
+    lb.load(cs.sm->limb[0], cs.sm->limb[1], cs.sm->limb[2], cs.lane, inv);
+    const uint8_t* st[MAXCH];
+#pragma unroll
+    for (int q = 0; q < MAXCH; ++q) st[q] = q < nch ? cs.wait_at(c, q, 2) : nullptr;
+    int acc[4][3];
+    const uint4* rowp[4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int i = cs.warp + NCW * r;
+        const uint8_t* ch = i < n ? pick(st, i / PPC) : nullptr;
+        const int q = i / PPC, nin = min(PPC, n - q * PPC);
+        rowp[2 * r] = ch ? reinterpret_cast<const uint4*>(ch + (size_t)(i - q * PPC) * RS) : nullptr;
+        rowp[2 * r + 1] = ch ? reinterpret_cast<const uint4*>(ch + (size_t)(nin + i - q * PPC) * RS) : nullptr;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = acc[r][2] = 0;
+#pragma unroll
+    for (int j = 0; j < UPL; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (rowp[r]) lb.acc(rowp[r][cs.lane + 32 * j], j, acc[r][0], acc[r][1], acc[r][2]);
+    float v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = limb_sum_f32(acc[r][0], acc[r][1], acc[r][2]);
+    const float tot = xreduce<4>(v, cs.lane);          // lane 8 m + {0..7}: row m = (g0, u0, g1, u1)
+    const float upv = __shfl_down_sync(0xffffffffu, tot, 8);
+    const int i = cs.warp + NCW * (cs.lane >> 4);
+    if ((cs.lane & 15) == 0 && i < n) out(p0 + i, val(tot * inv * sg[i], upv * inv * su[i]));
+    cs.release_n(nch);
 }
 
 __device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layer, int e) {
@@ -875,33 +1100,40 @@ __device__ __forceinline__ void stage_scales(const DecodeParams& P, const Cons& 
 template <class WT>
 __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint32_t epoch, int token,
                               unsigned long long& cta_key) {
+    constexpr bool L8 = WT::LIMBS;
     Smem* sm = c.sm;
     Cons cs{sm, 0u, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), (int)threadIdx.x};
     Workspace* ws = c.ws;
     const bool cta0 = G.b == 0;
     stage_pointers(P, cs, WT::HAS_SCALE);
+    for (int i = cs.tid; i < INTER / 4; i += NCT) sm->limb[3][i] = 0;   // zero B columns of the LM-head mma
     consumers_sync();
     if (WT::HAS_SCALE) stage_scales(P, cs, G);
-    NormW w_in, w_post;
+    NormW4 w_in, w_post;
     w_in.load(cs, sm->lw[0][LW_IN]);
-    if (!*(volatile int*)&sm->abort_flag) {
-        const __nv_bfloat16* er = (const __nv_bfloat16*)P.embed + (size_t)token * HIDDEN;
-        for (int i = cs.tid; i < HIDDEN; i += NCT) sm->h[i] = __bfloat162float(er[i]);
+    InputScale xin{1.f, 1.f};
+    {   // layer-0 input: the embedding row (no exchange)
+        uint32_t pay[1][4] = {{0u, 0u, 0u, 0u}};
+        if (cs.tid < HIDDEN / 4 && !*(volatile int*)&sm->abort_flag) {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>((const __nv_bfloat16*)P.embed + (size_t)token * HIDDEN) + cs.tid);
+            pay[0][0] = u.x & 0xffffu; pay[0][1] = u.x >> 16; pay[0][2] = u.y & 0xffffu; pay[0][3] = u.y >> 16;
+        }
+        xin = finish_input<1, L8, true>(cs, pay, HIDDEN / 4, true, w_in, sm->x, sm->h);
     }
     for (int l = 0; l < P.L; ++l) {
         const int par = l & 1;
         const int tb = l * TRACE_PER_LAYER;
-        if (consumers_sync_abort(c)) break;
         if (l > 0) {
-            float* lh = (cta0 && P.layer_hidden) ? P.layer_hidden + (size_t)(l - 1) * HIDDEN : nullptr;
-            poll_block<NORM_PER>(c, cs, ws->xh[par], HIDDEN, tag_of(epoch, l, E_H), 20, [&](int i, uint32_t p) {
-                const float v = bf16_bits_to_f32(p);
-                sm->h[i] = v;
-                if (lh) lh[i] = v;
-            });
+            if (consumers_sync_abort(c)) break;
+            uint32_t pay[1][4];
+            poll_groups<1>(c, cs, ws->xh[par], HIDDEN / 4, tag_of(epoch, l, E_H), 20, pay);
+            if (cta0 && P.layer_hidden && cs.tid < HIDDEN / 4) {
+                float* lh = P.layer_hidden + (size_t)(l - 1) * HIDDEN + 4 * cs.tid;
+                for (int e = 0; e < 4; ++e) lh[e] = bf16_bits_to_f32(pay[0][e] & 0xffffu);
+            }
+            xin = finish_input<1, L8, true>(cs, pay, HIDDEN / 4, true, w_in, sm->x, sm->h);
         }
         trace_stamp(P, cs, tb + TR_START);
-        rmsnorm_1024(cs, sm->h, w_in, sm->x);
         w_post.load(cs, sm->lw[l][LW_POST]);  // needed after attention: its latency is hidden
         const float* lsc = sm->scl + l * SCL_STRIDE;
         // --- QKV ---
@@ -909,11 +1141,13 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
             const uint32_t t = tag_of(epoch, l, E_QKV);
             const bool skip = (l == 0 && G.b == P.skip_cta);
             uint64_t* dst = ws->xqkv[par];
-            auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[r - G.qkv0] : 1.f; };
+            const float rstd = xin.rstd;
+            auto scl = [&](int r) { return (WT::HAS_SCALE ? lsc[r - G.qkv0] : 1.f) * rstd; };
             auto out = [&](int r, float d) {
                 if (!skip) st_tagged(&dst[r], t, __float_as_uint(d));
             };
-            mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, scl, out);
+            if constexpr (L8) mv_rows8<HIDDEN, 3, 2>(c, cs, G.qkv0, G.qkv1, xin.inv, scl, out);
+            else mv_phase<WT, HIDDEN>(c, cs, G.qkv0, G.qkv1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_QKV);
         // --- attention (only CTAs that own an item) ---
@@ -924,47 +1158,63 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
         }
         // --- O projection + residual ---
         if (consumers_sync_abort(c)) break;
-        poll_block<QSZ / NCT + 1>(c, cs, ws->xattn[par], QSZ, tag_of(epoch, l, E_ATTN), 30,
-                                  [&](int i, uint32_t p) { sm->x[i] = __uint_as_float(p); });
-        consumers_sync();
+        {
+            uint32_t pay[2][4];
+            poll_groups<2>(c, cs, ws->xattn[par], QSZ / 4, tag_of(epoch, l, E_ATTN), 30, pay);
+            const NormW4 one{};
+            xin = finish_input<2, L8, false>(cs, pay, QSZ / 4, false, one, sm->x, nullptr);
+        }
         trace_stamp(P, cs, tb + TR_OIN);
         {
             const uint32_t t = tag_of(epoch, l, E_ACT);
             uint64_t* dst = ws->xact[par];
             auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_O + r - G.o0] : 1.f; };
             auto out = [&](int r, float d) { st_tagged(&dst[r], t, __float_as_uint(d + sm->h[r])); };
-            mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, scl, out);
+            if constexpr (L8) mv_rows8<QSZ, 1, 1>(c, cs, G.o0, G.o1, xin.inv, scl, out);
+            else mv_phase<WT, QSZ>(c, cs, G.o0, G.o1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_O);
         // --- post-attention norm + gate/up ---
         if (consumers_sync_abort(c)) break;
-        poll_block<NORM_PER>(c, cs, ws->xact[par], HIDDEN, tag_of(epoch, l, E_ACT), 40,
-                             [&](int i, uint32_t p) { sm->act[i] = __uint_as_float(p); });
-        rmsnorm_1024(cs, sm->act, w_post, sm->x);
+        {
+            uint32_t pay[1][4];
+            poll_groups<1>(c, cs, ws->xact[par], HIDDEN / 4, tag_of(epoch, l, E_ACT), 40, pay);
+            xin = finish_input<1, L8, true>(cs, pay, HIDDEN / 4, false, w_post, sm->x, sm->act);
+        }
         w_in.load(cs, l + 1 < P.L ? sm->lw[l + 1][LW_IN] : P.final_norm);  // next norm, loaded ahead
         trace_stamp(P, cs, tb + TR_NORM2);
         {
             const uint32_t t = tag_of(epoch, l, E_MLP);
             uint64_t* dst = ws->xmlp[par];
-            auto out = [&](int r, float gd, float ud) {
+            const float rstd = xin.rstd;
+            auto val = [&](float gd, float ud) {
+                gd *= rstd;
+                ud *= rstd;
                 const float silu = gd / (1.0f + expf(-gd));
-                st_tagged(&dst[r], t, __float_as_uint(silu * ud));
+                return silu * ud;
             };
-            gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, lsc + SCL_G, lsc + SCL_U, out);
+            auto out = [&](int r, float gd, float ud) { st_tagged(&dst[r], t, __float_as_uint(val(gd, ud))); };
+            auto pubf = [&](int r, float v) { st_tagged(&dst[r], t, __float_as_uint(v)); };
+            if constexpr (L8) gu_rows8<3>(c, cs, G.gu0, G.gu1, xin.inv, lsc + SCL_G, lsc + SCL_U, val, pubf);
+            else gu_phase<WT>(c, cs, G.gu0, G.gu1, sm->x, lsc + SCL_G, lsc + SCL_U, out);
         }
         trace_stamp(P, cs, tb + TR_GU);
         // --- down + residual -> next h (bf16) ---
         if (consumers_sync_abort(c)) break;
-        poll_block<INTER / NCT>(c, cs, ws->xmlp[par], INTER, tag_of(epoch, l, E_MLP), 50,
-                                [&](int i, uint32_t p) { sm->x[i] = __uint_as_float(p); });
-        consumers_sync();
+        {
+            uint32_t pay[2][4];
+            poll_groups<2>(c, cs, ws->xmlp[par], INTER / 4, tag_of(epoch, l, E_MLP), 50, pay);
+            const NormW4 one{};
+            xin = finish_input<2, L8, false>(cs, pay, INTER / 4, false, one, sm->x, nullptr);
+        }
         trace_stamp(P, cs, tb + TR_MLPIN);
         {
             const uint32_t t = tag_of(epoch, l + 1, E_H);
             uint64_t* dst = ws->xh[(l + 1) & 1];
             auto scl = [&](int r) { return WT::HAS_SCALE ? lsc[SCL_D + r - G.d0] : 1.f; };
             auto out = [&](int r, float d) { st_tagged(&dst[r], t, f32_to_bf16_bits(d + sm->act[r])); };
-            mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, scl, out);
+            if constexpr (L8) mv_rows8<INTER, 1, 2>(c, cs, G.d0, G.d1, xin.inv, scl, out);
+            else mv_phase<WT, INTER>(c, cs, G.d0, G.d1, sm->x, scl, out);
         }
         trace_stamp(P, cs, tb + TR_DOWN);
     }
@@ -972,27 +1222,28 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     cta_key = 0ull;
     if (consumers_sync_abort(c)) return;
     {
-        float* lh = (cta0 && P.layer_hidden) ? P.layer_hidden + (size_t)(P.L - 1) * HIDDEN : nullptr;
-        poll_block<NORM_PER>(c, cs, ws->xh[P.L & 1], HIDDEN, tag_of(epoch, P.L, E_H), 60, [&](int i, uint32_t p) {
-            const float v = bf16_bits_to_f32(p);
-            sm->h[i] = v;
-            if (lh) lh[i] = v;
-        });
+        uint32_t pay[1][4];
+        poll_groups<1>(c, cs, ws->xh[P.L & 1], HIDDEN / 4, tag_of(epoch, P.L, E_H), 60, pay);
+        if (cta0 && P.layer_hidden && cs.tid < HIDDEN / 4) {
+            float* lh = P.layer_hidden + (size_t)(P.L - 1) * HIDDEN + 4 * cs.tid;
+            for (int e = 0; e < 4; ++e) lh[e] = bf16_bits_to_f32(pay[0][e] & 0xffffu);
+        }
+        xin = finish_input<1, L8, true>(cs, pay, HIDDEN / 4, true, w_in, sm->x, sm->h);
     }
     trace_stamp(P, cs, P.L * TRACE_PER_LAYER + 0);
-    rmsnorm_1024(cs, sm->h, w_in, sm->x);
     if (cta0 && P.g_normalized)
-        for (int i = cs.tid; i < HIDDEN; i += NCT) P.g_normalized[i] = sm->x[i];
+        for (int i = cs.tid; i < HIDDEN; i += NCT) P.g_normalized[i] = sm->x[i] * xin.rstd;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     {
         float* logits = P.logits;
-        auto scl = [&](int r) { return WT::HAS_SCALE ? sm->lm_scl[r - G.lm0] : 1.f; };
+        const float rstd = xin.rstd;
+        auto scl = [&](int r) { return (WT::HAS_SCALE ? sm->lm_scl[r - G.lm0] : 1.f) * rstd; };
         auto out = [&](int r, float d) {
             if (logits) logits[r] = d;
             if (d > best_v || (d == best_v && r < best_i)) { best_v = d; best_i = r; }
         };
-        if constexpr (WT::LIMBS) mma_stream<HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, out);
+        if constexpr (L8) mma_stream<HIDDEN>(c, cs, G.lm0, G.lm1, xin.inv, scl, out);
         else mv_phase<WT, HIDDEN>(c, cs, G.lm0, G.lm1, sm->x, scl, out);
     }
     // argmax over the lanes of the warp (ties: lowest row)
@@ -1106,8 +1357,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) matvec_kernel(const MatvecParams 
         float* y = P.y;
         auto scl = [&](int r) { return WT::HAS_SCALE ? __ldg(sc + r) : 1.f; };
         auto out = [&](int r, float d) { y[r] = d; };
-        if constexpr (WT::LIMBS) mma_stream<K>(c, cs, r0, r1, sm->x, scl, out);
-        else mv_phase<WT, K>(c, cs, r0, r1, sm->x, scl, out);
+        if constexpr (WT::LIMBS) {
+            build_limbs(cs, sm->x, K);
+            mma_stream<K>(c, cs, r0, r1, sm->limb_inv, scl, out);
+        } else {
+            mv_phase<WT, K>(c, cs, r0, r1, sm->x, scl, out);
+        }
     }
     __syncthreads();
 }

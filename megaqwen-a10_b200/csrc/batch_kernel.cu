@@ -421,6 +421,10 @@ __device__ bool tc_gemm(Ctx& c, const uint8_t* xa, int K, int nt, TilePtr tile_p
     const uint32_t tx = (uint32_t)(AB + BR);
     const int SB = (AB + 3 * N * KS + 1023) & ~1023;
     const int nr = min(NR, RING / SB);
+    if (nr < NMMA) {   // the MMA issuers alternate slots: each needs one (static_asserts cover the shapes used)
+        if (threadIdx.x == 0) fail(c, MQ_DEV_RANGE, 299);
+        return false;
+    }
     const uint32_t par0 = c.upar;   // parity of the next use of each slot
     // parity of the mbarrier phases of slab s (its slot's (s / nr)-th use in this GEMM)
     auto par = [&](int s) { return ((par0 >> (s % nr)) ^ (uint32_t)(s / nr)) & 1u; };

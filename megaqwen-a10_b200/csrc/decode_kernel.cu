@@ -523,41 +523,6 @@ __device__ __forceinline__ void mma_stream(Ctx& c, Cons& cs, int r0, int r1, flo
     }
 }
 
-// Gather n tagged words addr(0..n) into the consumer threads: thread t owns
-// indices t, t + NCT, ...; all of its loads are issued together and only the
-// words whose tag has not arrived are re-read.  store(i, payload) per word.
-template <int MAXK, class Addr, class Store>
-__device__ __forceinline__ void poll_gather(Ctx& c, const Cons& cs, Addr addr, int n, uint32_t tag, int where,
-                                            Store store) {
-    uint64_t v[MAXK];
-#pragma unroll
-    for (int k = 0; k < MAXK; ++k) {
-        const int i = cs.tid + k * NCT;
-        v[k] = i < n ? ld_relaxed64(addr(i)) : ((uint64_t)tag << 32);
-    }
-    bool done = false;
-    unsigned long long t0 = 0;
-    for (uint32_t it = 0; !done; ++it) {
-        done = true;
-#pragma unroll
-        for (int k = 0; k < MAXK; ++k) {
-            if ((uint32_t)(v[k] >> 32) != tag) {
-                done = false;
-                v[k] = ld_relaxed64(addr(cs.tid + k * NCT));
-            }
-        }
-        if (!done && (it & 127) == 127) {
-            if (t0 == 0) t0 = globaltimer();
-            if (aborted(c)) break;
-            if (globaltimer() - t0 > c.budget) { record_error(c, MQ_DEV_TIMEOUT_EXCHANGE, where); break; }
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < MAXK; ++k) {
-        const int i = cs.tid + k * NCT;
-        if (i < n) store(i, (uint32_t)v[k]);
-    }
-}
 
 
 // ---------------------------------------------------------------------------
@@ -582,14 +547,14 @@ __device__ __forceinline__ void ld_relaxed_v4(const uint64_t* p, uint64_t (&v)[4
 
 // Each 8-byte word of the vector access is single-copy atomic, so a word's tag
 // and payload arrive together.
-template <int MAXG>
-__device__ __forceinline__ void poll_groups(Ctx& c, const Cons& cs, const uint64_t* base, int ngroups, uint32_t tag,
-                                            int where, uint32_t (&pay)[MAXG][4]) {
+template <int MAXG, class Addr>
+__device__ __forceinline__ void poll_groups_at(Ctx& c, const Cons& cs, Addr addr, int ngroups, uint32_t tag,
+                                               int where, uint32_t (&pay)[MAXG][4]) {
     uint64_t v[MAXG][4];
 #pragma unroll
     for (int k = 0; k < MAXG; ++k) {
         const int g = cs.tid + k * NCT;
-        if (g < ngroups) ld_relaxed_v4(base + 4 * g, v[k]);
+        if (g < ngroups) ld_relaxed_v4(addr(g), v[k]);
         else v[k][0] = v[k][1] = v[k][2] = v[k][3] = (uint64_t)tag << 32;
     }
     unsigned long long t0 = 0;
@@ -601,7 +566,7 @@ __device__ __forceinline__ void poll_groups(Ctx& c, const Cons& cs, const uint64
             if ((uint32_t)(v[k][0] >> 32) != tag || (uint32_t)(v[k][1] >> 32) != tag ||
                 (uint32_t)(v[k][2] >> 32) != tag || (uint32_t)(v[k][3] >> 32) != tag) {
                 done = false;
-                ld_relaxed_v4(base + 4 * g, v[k]);
+                ld_relaxed_v4(addr(g), v[k]);
             }
         }
         if (done) break;
@@ -615,6 +580,13 @@ __device__ __forceinline__ void poll_groups(Ctx& c, const Cons& cs, const uint64
     for (int k = 0; k < MAXG; ++k)
 #pragma unroll
         for (int e = 0; e < 4; ++e) pay[k][e] = (uint32_t)v[k][e];
+}
+
+// addr(g): the 4 consecutive words of group g.
+template <int MAXG>
+__device__ __forceinline__ void poll_groups(Ctx& c, const Cons& cs, const uint64_t* base, int ngroups, uint32_t tag,
+                                            int where, uint32_t (&pay)[MAXG][4]) {
+    poll_groups_at<MAXG>(c, cs, [&](int g) { return base + 4 * g; }, ngroups, tag, where, pay);
 }
 
 struct InputScale {
@@ -881,10 +853,15 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
     {
         const uint64_t* xq = c.ws->xqkv[par];
         const int g = G.g;
-        poll_gather<2>(c, cs, [&](int i) {
+        uint32_t pay[1][4];
+        poll_groups_at<1>(c, cs, [&](int gr) {
+            const int i = 4 * gr;   // the three runs are 4-word aligned
             return xq + (i < 2 * HD ? 2 * g * HD + i
                                     : (i < 3 * HD ? QSZ + g * HD + (i - 2 * HD) : QSZ + KVSZ + g * HD + (i - 3 * HD)));
-        }, 4 * HD, tq, 10, [&](int i, uint32_t p) { sm->raw[i] = __uint_as_float(p); });
+        }, HD, tq, 10, pay);
+        if (cs.tid < HD)
+            *reinterpret_cast<float4*>(sm->raw + 4 * cs.tid) = make_float4(
+                __uint_as_float(pay[0][0]), __uint_as_float(pay[0][1]), __uint_as_float(pay[0][2]), __uint_as_float(pay[0][3]));
     }
     consumers_sync();
     if (cs.warp < 2) {

@@ -121,13 +121,16 @@ class OracleDecoder:
                     q, s = quantize_per_channel(w)
                     d[proj] = ("int8", q.float(), s)   # fp32 copy of the int8 codes
                 else:
-                    d[proj] = ("bf16", w, None)
+                    # fp32 copy of the bf16 weights, made once: the BF16 kernel's
+                    # math (bf16 weights, fp32 activations and accumulation) on
+                    # exactly representable values; converting per step would only be slower
+                    d[proj] = ("bf16", w.float() if not quantized else w, None)
             self.layers.append(d)
         if quantized:
             q, s = quantize_per_channel(lm)
             self.lm = ("int8", q.float(), s)
         else:
-            self.lm = ("bf16", lm, None)
+            self.lm = ("bf16", lm.float(), None)
         self.cos, self.sin = rope_tables(max_seq_len, theta=rope_theta)
         self.reset()
 
@@ -144,7 +147,7 @@ class OracleDecoder:
             return (w @ xx) * s
         if self.quantized:
             return matvec_bf16(x, w)            # QwenDecoder's bf16 q/k/v
-        return w.float() @ x.float()            # BF16 kernel: fp32 activations
+        return w @ x.float()                    # BF16 kernel: fp32 weights (exact bf16) x fp32 activations
 
     def attention(self, q_rope, li, cache_len):
         """int8_decoder.py:242-255."""

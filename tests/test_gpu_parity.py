@@ -172,7 +172,7 @@ def test_decode_bf16_two_layers_teacher_forced(small_state):
     assert agree >= 0.95 * steps
 
 
-@pytest.mark.parametrize("ctx", [700, 4096])
+@pytest.mark.parametrize("ctx", [700, 4096, 16384, 32768])
 def test_long_context_split_attention(small_state, ctx):
     """Pre-filled random KV cache (N(0,1) bf16) -> one step at position ctx
     exercises the split-K attention merge."""

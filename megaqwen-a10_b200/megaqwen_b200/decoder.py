@@ -364,6 +364,20 @@ class A10Decoder:
 
     def __init__(self, state, quantized=True, max_seq_len=MAX_SEQ_LEN, num_layers=NUM_LAYERS, device="cuda",
                  tokenizer=None, quantized_state=None):
+        import os
+        if isinstance(state, (str, os.PathLike)):
+            # The reference's constructor shape A10Decoder(model_path, max_seq_len)
+            # (a10_decode.py:35-36): a checkpoint directory, and an int second
+            # positional argument is the sequence limit.
+            if not isinstance(quantized, bool):
+                max_seq_len, quantized = int(quantized), True
+            from . import checkpoint as ck
+            path = os.fspath(state)
+            if tokenizer is None and (os.path.exists(os.path.join(path, "tokenizer.json")) or
+                                      os.path.exists(os.path.join(path, "tokenizer_config.json"))):
+                from transformers import AutoTokenizer
+                tokenizer = AutoTokenizer.from_pretrained(path, local_files_only=True)
+            state = ck.load_state(path, num_layers=num_layers)
         self.device = torch.device(device)
         self.max_seq_len = max_seq_len
         self.tokenizer = tokenizer

@@ -83,6 +83,9 @@ def test_from_pretrained_decodes_like_in_memory(tmp_path):
     want = ref.generate(prompt, max_new_tokens=6)
     assert a.generate(prompt, max_new_tokens=6) == want
     assert b.generate(prompt, max_new_tokens=6) == want
+    # the reference's constructor shape: A10Decoder(model_path, max_seq_len)
+    c = mq.A10Decoder(str(tmp_path), 64, num_layers=L)
+    assert c.max_seq_len == 64 and c.generate(prompt, max_new_tokens=6) == want
 
 
 @pytest.mark.gpu

@@ -812,16 +812,20 @@ enum { E_H = 0, E_QKV = 1, E_PART = 2, E_ATTN = 3, E_ACT = 4, E_MLP = 5 };
 // (a10_int8_decode_kernel.cu:160-192, int8_decoder.py:234-240).  Lane holds
 // dims lane + 32j, so the RoPE partners (i, i+64) are j and j+2 of one lane.
 // Norm weights and the cos/sin row are loaded ahead of the exchange wait.
+// The weights and the cos/sin row are kept as raw bf16 bits until use: converting
+// them at load time would stall the warp on the loads before its exchange poll.
 struct RopeRegs {
-    float nw[4], cs[4], sn[4];
+    uint16_t nw[4], cs[4], sn[4];
     __device__ __forceinline__ void load(const void* normw, const __nv_bfloat16* cosr, const __nv_bfloat16* sinr,
                                          int lane) {
-        const __nv_bfloat16* w = (const __nv_bfloat16*)normw;
+        const uint16_t* w = (const uint16_t*)normw;
+        const uint16_t* cr = (const uint16_t*)cosr;
+        const uint16_t* sr = (const uint16_t*)sinr;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            nw[j] = __bfloat162float(__ldg(w + lane + 32 * j));
-            cs[j] = __bfloat162float(__ldg(cosr + lane + 32 * j));
-            sn[j] = __bfloat162float(__ldg(sinr + lane + 32 * j));
+            nw[j] = __ldg(w + lane + 32 * j);
+            cs[j] = __ldg(cr + lane + 32 * j);
+            sn[j] = __ldg(sr + lane + 32 * j);
         }
     }
 };
@@ -833,11 +837,13 @@ __device__ __forceinline__ void qk_norm_rope(const float* raw, const RopeRegs& R
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)HD + RMS_EPS);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * R.nw[j];
+    for (int j = 0; j < 4; ++j) v[j] = v[j] * r * bf16_bits_to_f32(R.nw[j]);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-        out[j] = v[j] * R.cs[j] - v[j + 2] * R.sn[j];
-        out[j + 2] = v[j] * R.sn[j + 2] + v[j + 2] * R.cs[j + 2];
+        const float c0 = bf16_bits_to_f32(R.cs[j]), s0 = bf16_bits_to_f32(R.sn[j]);
+        const float c2 = bf16_bits_to_f32(R.cs[j + 2]), s2 = bf16_bits_to_f32(R.sn[j + 2]);
+        out[j] = v[j] * c0 - v[j + 2] * s0;
+        out[j + 2] = v[j] * s2 + v[j + 2] * c2;
     }
 }
 

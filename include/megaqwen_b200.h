@@ -358,8 +358,9 @@ int mq_inject_skip_publish(int enable, int cta);
  * %globaltimer stamps (ns) into dev_buf[cta * slots_per_cta + slot], slot =
  * layer * 10 + event (events: 0 layer input ready, 1 QKV published, 2 attention
  * published, 3 attention gathered, 4 O published, 5 post-norm done, 6 gate/up
- * published, 7 MLP gathered, 8 down published; slots num_layers*10 + 0/1: final
- * hidden gathered / LM head done).  NULL disables.  No reference counterpart
+ * published, 7 MLP gathered, 8 down published; slots num_layers*10 + 0/1/2/3:
+ * final hidden gathered / LM head done / CTA entered the kernel / CTA done).
+ * NULL disables.  No reference counterpart
  * (the reference has no tracing). */
 int mq_set_trace(unsigned long long* dev_buf, int slots_per_cta);
 

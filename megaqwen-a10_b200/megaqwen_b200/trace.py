@@ -18,7 +18,7 @@ PER_LAYER = 10
 def capture_step(decoder, token=5):
     """Runs one decode step of `decoder` with tracing; returns an int64 [num_ctas, slots] CPU tensor."""
     n = _lib.kernel_info()["num_ctas"]
-    slots = PER_LAYER * (decoder.num_layers_ + 1)
+    slots = PER_LAYER * (decoder.num_layers_ + 1)   # the last group: final hidden, LM head, entry, exit
     buf = torch.zeros(n, slots, dtype=torch.int64, device=decoder.device)
     _lib.set_trace(buf, slots)
     try:
@@ -51,7 +51,14 @@ def summarize(stamps, num_layers):
                 d.append(a - b)
         if d:
             phase[PHASES[e]] = statistics.median(d)
+    def colmin(c):
+        col = rel[:, c]
+        col = col[~torch.isnan(col)]
+        return float(col.min()) if len(col) else float("nan")
+
     return {"layer_us_median": statistics.median(layer) if layer else None,
             "phase_us_median": phase,
+            "kernel_entry_us": colmin(num_layers * PER_LAYER + 2),      # first CTA entered (negative: before layer 0)
             "final_hidden_us": colmax(num_layers * PER_LAYER),
-            "lm_head_done_us": colmax(num_layers * PER_LAYER + 1)}
+            "lm_head_done_us": colmax(num_layers * PER_LAYER + 1),
+            "kernel_done_us": colmax(num_layers * PER_LAYER + 3)}      # last CTA done

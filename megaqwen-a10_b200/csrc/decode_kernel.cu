@@ -1042,42 +1042,80 @@ enum { LS_Q = 0, LS_K, LS_V, LS_O, LS_G, LS_U, LS_D };
 // per pointer at kernel start instead of one per phase).
 __device__ __forceinline__ void stage_pointers(const DecodeParams& P, const Cons& cs, bool scaled) {
     const int per = scaled ? 18 : 11;
-    for (int i = cs.tid; i < P.L * per; i += NCT) {
-        const int l = i / per, f = i % per;
-        if (f < 11) cs.sm->lw[l][f] = reinterpret_cast<const void* const*>(&P.layers[l])[f];
-        else cs.sm->ls[l][f - 11] = reinterpret_cast<float* const*>(&P.scales[l])[f - 11];
+    constexpr int MAXI = (MAX_LAYERS * 18 + NCT - 1) / NCT;
+    const void* v[MAXI];
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {   // all loads first, so they are in flight together
+        const int i = cs.tid + k * NCT;
+        v[k] = nullptr;
+        if (i < P.L * per) {
+            const int l = i / per, f = i % per;
+            v[k] = f < 11 ? reinterpret_cast<const void* const*>(&P.layers[l])[f]
+                          : reinterpret_cast<const void* const*>(&P.scales[l])[f - 11];
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+        const int i = cs.tid + k * NCT;
+        if (i < P.L * per) {
+            const int l = i / per, f = i % per;
+            if (f < 11) cs.sm->lw[l][f] = v[k];
+            else cs.sm->ls[l][f - 11] = reinterpret_cast<const float*>(v[k]);
+        }
     }
 }
 
 // Every per-row scale this CTA will need in the step, into shared memory, so
 // that no matvec row waits on a dependent global load.  Needs the staged
-// pointer tables (call after stage_pointers + a consumer barrier).
+// pointer tables (call after stage_pointers + a consumer barrier).  Each thread
+// issues all of its loads before it stores any, so their latencies overlap.
 __device__ __forceinline__ void stage_scales(const DecodeParams& P, const Cons& cs, const Geo& G) {
     Smem* sm = cs.sm;
-    for (int i = cs.tid; i < P.L * SCL_STRIDE; i += NCT) {
-        const int l = i / SCL_STRIDE, j = i % SCL_STRIDE;
-        float v = 0.f;
-        if (j < SCL_O) {
-            const int r = G.qkv0 + j;
-            if (r < G.qkv1)
-                v = __ldg(r < QSZ ? sm->ls[l][LS_Q] + r
-                                  : (r < QSZ + KVSZ ? sm->ls[l][LS_K] + (r - QSZ) : sm->ls[l][LS_V] + (r - QSZ - KVSZ)));
-        } else if (j < SCL_G) {
-            const int r = G.o0 + (j - SCL_O);
-            if (r < G.o1) v = __ldg(sm->ls[l][LS_O] + r);
-        } else if (j < SCL_U) {
-            const int r = G.gu0 + (j - SCL_G);
-            if (r < G.gu1) v = __ldg(sm->ls[l][LS_G] + r);
-        } else if (j < SCL_D) {
-            const int r = G.gu0 + (j - SCL_U);
-            if (r < G.gu1) v = __ldg(sm->ls[l][LS_U] + r);
-        } else {
-            const int r = G.d0 + (j - SCL_D);
-            if (r < G.d1) v = __ldg(sm->ls[l][LS_D] + r);
+    constexpr int MAXI = (MAX_LAYERS * SCL_STRIDE + NCT - 1) / NCT;
+    constexpr int MAXJ = (LM_MAXR + NCT - 1) / NCT;
+    float v[MAXI], w[MAXJ];
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+        const int i = cs.tid + k * NCT;
+        const float* src = nullptr;
+        if (i < P.L * SCL_STRIDE) {
+            const int l = i / SCL_STRIDE, j = i % SCL_STRIDE;
+            if (j < SCL_O) {
+                const int r = G.qkv0 + j;
+                if (r < G.qkv1)
+                    src = r < QSZ ? sm->ls[l][LS_Q] + r
+                                  : (r < QSZ + KVSZ ? sm->ls[l][LS_K] + (r - QSZ) : sm->ls[l][LS_V] + (r - QSZ - KVSZ));
+            } else if (j < SCL_G) {
+                const int r = G.o0 + (j - SCL_O);
+                if (r < G.o1) src = sm->ls[l][LS_O] + r;
+            } else if (j < SCL_U) {
+                const int r = G.gu0 + (j - SCL_G);
+                if (r < G.gu1) src = sm->ls[l][LS_G] + r;
+            } else if (j < SCL_D) {
+                const int r = G.gu0 + (j - SCL_U);
+                if (r < G.gu1) src = sm->ls[l][LS_U] + r;
+            } else {
+                const int r = G.d0 + (j - SCL_D);
+                if (r < G.d1) src = sm->ls[l][LS_D] + r;
+            }
         }
-        sm->scl[i] = v;
+        v[k] = src ? __ldg(src) : 0.f;
     }
-    for (int j = cs.tid; j < G.lm1 - G.lm0; j += NCT) sm->lm_scl[j] = __ldg(P.lm_scale + G.lm0 + j);
+#pragma unroll
+    for (int k = 0; k < MAXJ; ++k) {
+        const int j = cs.tid + k * NCT;
+        w[k] = j < G.lm1 - G.lm0 ? __ldg(P.lm_scale + G.lm0 + j) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+        const int i = cs.tid + k * NCT;
+        if (i < P.L * SCL_STRIDE) sm->scl[i] = v[k];
+    }
+#pragma unroll
+    for (int k = 0; k < MAXJ; ++k) {
+        const int j = cs.tid + k * NCT;
+        if (j < G.lm1 - G.lm0) sm->lm_scl[j] = w[k];
+    }
 }
 
 template <class WT>
@@ -1254,6 +1292,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem* sm = reinterpret_cast<Smem*>(smem_raw);
     Ctx c{sm, P.ws, P.budget_ns};
+    if (P.trace && threadIdx.x == 0 && P.L * TRACE_PER_LAYER + 3 < P.trace_slots)   // kernel entry
+        P.trace[(size_t)blockIdx.x * P.trace_slots + P.L * TRACE_PER_LAYER + 2] = globaltimer();
     Geo G;
     G.init(P);
     const uint32_t epoch = ld_relaxed32(&P.ws->epoch);
@@ -1296,6 +1336,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
             atomicExch(&ws->epoch, epoch + (uint32_t)(P.L + 1) * TAGS_PER_LAYER);
             __threadfence();
         }
+        if (P.trace && P.L * TRACE_PER_LAYER + 3 < P.trace_slots)   // CTA done
+            P.trace[(size_t)blockIdx.x * P.trace_slots + P.L * TRACE_PER_LAYER + 3] = globaltimer();
     }
 }
 

@@ -12,7 +12,8 @@ from .decoder import A10Decoder, A10Int8MegakernelDecoder, A10MegakernelDecoder,
 from .batch import BatchedDecoder, batch_matmul, pack_tiles
 from . import _lib, checkpoint
 from ._lib import MQError
+from .chat import A10Chat
 
 __all__ = ["CFG", "Qwen3Config", "quantize_per_channel", "quantize_state", "make_rope", "make_synthetic_state",
            "A10Decoder", "A10Int8MegakernelDecoder", "A10MegakernelDecoder", "BatchedDecoder", "batch_matmul", "pack_tiles", "layer_lists",
-           "MQError"]
+           "MQError", "A10Chat"]

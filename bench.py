@@ -619,10 +619,13 @@ def main():
         return
     if args.trace:
         from megaqwen_b200 import trace
-        dec = build_decoder(args.layers, 256)
-        for p in (int(x) for x in args.trace_pos.split(",")):
+        tpos = [int(x) for x in args.trace_pos.split(",")]
+        dec = build_decoder(args.layers, max(256, max(tpos) + 8))
+        for p in tpos:
             dec.reset()
-            if p:
+            if p > 256:       # long context: a zero cache of p positions times the same as a decoded one
+                dec.set_position(p)
+            elif p:
                 dec.decode_steps(5, p)
             torch.cuda.synchronize()
             out = trace.summarize(trace.capture_step(dec), args.layers)

@@ -93,6 +93,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+// n arrivals at once (completes the phase of a barrier initialised with count n)
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
                  : "memory");

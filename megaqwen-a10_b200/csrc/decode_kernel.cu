@@ -280,6 +280,17 @@ struct Cons {
         if (lane == 0) mbar_arrive(&sm->empty[seq % NSTAGE]);
         ++seq;
     }
+    // A chunk that only this warp reads: its arrival stands for all NCW warps, and
+    // the other warps step past it with skip(), so the stage is free as soon as
+    // its one reader is done with it.
+    // Used only where every chunk of a stage has the same single reader: a reader that
+    // skipped ahead could otherwise test a stage's parity a whole ring early.
+    __device__ void release_owned() {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cnt(&sm->empty[seq % NSTAGE], NCW);
+        ++seq;
+    }
+    __device__ void skip() { ++seq; }
     // The q-th chunk after the next one (q = 0 is what wait() would return).
     __device__ const uint8_t* wait_at(Ctx& c, uint32_t q, int where) {
         const uint32_t s = seq + q, stage = s % NSTAGE;
@@ -896,45 +907,65 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         }
     }
     consumers_sync();
-    // Flash-decode inside the CTA without block barriers.  Warp w owns the item's
-    // ring chunks ci with ci % NCW == w (32 positions each) and keeps its own
-    // online-softmax state (m, l, acc) for both GQA heads.  Within a chunk lane p
-    // scores position p over all 128 dims (dims visited in a lane-rotated order
-    // so the 32 lanes hit different banks), one max/sum reduction per chunk, and
-    // P.V is accumulated with lane holding dims 4*lane .. 4*lane+3.
+    // Flash-decode inside the CTA without block barriers.  On long splits warp w owns
+    // the ring chunks (32 positions each) that land in stages s with s % NCW == w and
+    // keeps its own online-softmax state (m, l, acc) for both GQA heads.  Within a
+    // chunk lane (g, h) scores positions 2g, 2g+1 over dims 64h .. 64h+63 (dims
+    // visited in a lane-rotated order so the lanes hit different banks), one
+    // max/sum reduction per chunk, and P.V is accumulated with lane holding dims
+    // 4*lane .. 4*lane+3.
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     const float scale = P.attn_scale;
     const float4* q0v = reinterpret_cast<const float4*>(sm->q[0]);
     const float4* q1v = reinterpret_cast<const float4*>(sm->q[1]);
     auto chunk = [&](const uint16_t* kb, const uint16_t* vb, int n) {
-        float s0 = -INFINITY, s1 = -INFINITY;
-        if (cs.lane < n) {
-            const uint16_t* kr = kb + cs.lane * HD;
-            float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+        // Lane (g, h) = (lane % 16, lane / 16) scores positions 2g and 2g+1 over dims
+        // 64h .. 64h+63 (one q load serves two positions); one shuffle joins the halves.
+        const int g = cs.lane & 15, dh = cs.lane >> 4;
+        const int pa = 2 * g, pb = pa + 1;
+        float sa0 = -INFINITY, sa1 = -INFINITY, sb0 = -INFINITY, sb1 = -INFINITY;
+        {
+            const uint16_t* ka = kb + (pa < n ? pa : 0) * HD + dh * (HD / 2);
+            const uint16_t* kc = kb + (pb < n ? pb : 0) * HD + dh * (HD / 2);
+            const float4* qa = q0v + dh * (HD / 8);
+            const float4* qb = q1v + dh * (HD / 8);
+            float xa = 0.f, xb = 0.f, ya = 0.f, yb = 0.f, xa2 = 0.f, xb2 = 0.f, ya2 = 0.f, yb2 = 0.f;
 #pragma unroll 8
-            for (int i = 0; i < HD / 4; ++i) {
-                const int d4 = (cs.lane + i) & (HD / 4 - 1);
-                const uint2 kw = *reinterpret_cast<const uint2*>(kr + 4 * d4);
-                const float k0 = bf16_bits_to_f32(kw.x & 0xffffu), k1 = bf16_bits_to_f32(kw.x >> 16);
-                const float k2 = bf16_bits_to_f32(kw.y & 0xffffu), k3 = bf16_bits_to_f32(kw.y >> 16);
-                const float4 qa = q0v[d4], qb = q1v[d4];
-                x0 = fmaf(qa.x, k0, x0); x1 = fmaf(qa.y, k1, x1); x0 = fmaf(qa.z, k2, x0); x1 = fmaf(qa.w, k3, x1);
-                y0 = fmaf(qb.x, k0, y0); y1 = fmaf(qb.y, k1, y1); y0 = fmaf(qb.z, k2, y0); y1 = fmaf(qb.w, k3, y1);
+            for (int i = 0; i < HD / 8; ++i) {
+                const int d4 = (g + i) & (HD / 8 - 1);
+                const uint2 wa = *reinterpret_cast<const uint2*>(ka + 4 * d4);
+                const uint2 wb = *reinterpret_cast<const uint2*>(kc + 4 * d4);
+                const float4 q0 = qa[d4], q1 = qb[d4];
+                const float a0 = bf16_bits_to_f32(wa.x & 0xffffu), a1 = bf16_bits_to_f32(wa.x >> 16);
+                const float a2 = bf16_bits_to_f32(wa.y & 0xffffu), a3 = bf16_bits_to_f32(wa.y >> 16);
+                const float b0 = bf16_bits_to_f32(wb.x & 0xffffu), b1 = bf16_bits_to_f32(wb.x >> 16);
+                const float b2 = bf16_bits_to_f32(wb.y & 0xffffu), b3 = bf16_bits_to_f32(wb.y >> 16);
+                xa = fmaf(q0.x, a0, xa); xa2 = fmaf(q0.y, a1, xa2); xa = fmaf(q0.z, a2, xa); xa2 = fmaf(q0.w, a3, xa2);
+                ya = fmaf(q1.x, a0, ya); ya2 = fmaf(q1.y, a1, ya2); ya = fmaf(q1.z, a2, ya); ya2 = fmaf(q1.w, a3, ya2);
+                xb = fmaf(q0.x, b0, xb); xb2 = fmaf(q0.y, b1, xb2); xb = fmaf(q0.z, b2, xb); xb2 = fmaf(q0.w, b3, xb2);
+                yb = fmaf(q1.x, b0, yb); yb2 = fmaf(q1.y, b1, yb2); yb = fmaf(q1.z, b2, yb); yb2 = fmaf(q1.w, b3, yb2);
             }
-            s0 = (x0 + x1) * scale;
-            s1 = (y0 + y1) * scale;
+            xa += xa2; ya += ya2; xb += xb2; yb += yb2;
+            xa += __shfl_xor_sync(0xffffffffu, xa, 16);
+            ya += __shfl_xor_sync(0xffffffffu, ya, 16);
+            xb += __shfl_xor_sync(0xffffffffu, xb, 16);
+            yb += __shfl_xor_sync(0xffffffffu, yb, 16);
+            if (pa < n) { sa0 = xa * scale; sa1 = ya * scale; }
+            if (pb < n) { sb0 = xb * scale; sb1 = yb * scale; }
         }
-        const float n0 = fmaxf(m0, warp_max(s0)), n1 = fmaxf(m1, warp_max(s1));
+        const float n0 = fmaxf(m0, warp_max(fmaxf(sa0, sb0))), n1 = fmaxf(m1, warp_max(fmaxf(sa1, sb1)));
         const float c0 = expf(m0 - n0), c1 = expf(m1 - n1);   // 0 while m is still -inf
-        const float e0 = cs.lane < n ? expf(s0 - n0) : 0.f;
-        const float e1 = cs.lane < n ? expf(s1 - n1) : 0.f;
-        l0 = l0 * c0 + warp_sum(e0);
-        l1 = l1 * c1 + warp_sum(e1);
+        const float ea0 = pa < n ? expf(sa0 - n0) : 0.f, eb0 = pb < n ? expf(sb0 - n0) : 0.f;
+        const float ea1 = pa < n ? expf(sa1 - n1) : 0.f, eb1 = pb < n ? expf(sb1 - n1) : 0.f;
+        // lanes g and g + 16 hold the same weights: sum one half only
+        l0 = l0 * c0 + warp_sum(dh ? 0.f : ea0 + eb0);
+        l1 = l1 * c1 + warp_sum(dh ? 0.f : ea1 + eb1);
 #pragma unroll
         for (int j = 0; j < 4; ++j) { a0[j] *= c0; a1[j] *= c1; }
         auto pv = [&](int p) {
-            const float ep0 = __shfl_sync(0xffffffffu, e0, p), ep1 = __shfl_sync(0xffffffffu, e1, p);
+            const float ep0 = __shfl_sync(0xffffffffu, (p & 1) ? eb0 : ea0, p >> 1);
+            const float ep1 = __shfl_sync(0xffffffffu, (p & 1) ? eb1 : ea1, p >> 1);
             const uint2 vw = *reinterpret_cast<const uint2*>(vb + p * HD + 4 * cs.lane);
             const float v0 = bf16_bits_to_f32(vw.x & 0xffffu), v1 = bf16_bits_to_f32(vw.x >> 16);
             const float v2 = bf16_bits_to_f32(vw.y & 0xffffu), v3 = bf16_bits_to_f32(vw.y >> 16);
@@ -993,15 +1024,19 @@ MQ_PHASE void attention_item(const DecodeParams& P, Ctx& c, Cons& cs, const Geo&
         }
         if (G.owner && (G.past1 - G.past0) % NCW == cs.warp) one(sm->kvcur[0], sm->kvcur[1]);   // the current position
     } else {
-        int ci = 0;  // item-relative chunk index
-        for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS, ++ci) {
+        // Warp (stage % NCW) alone reads the chunks of a ring stage here, so a stage is
+        // free as soon as that warp is done with it, whatever the other warps are doing.
+        for (int p = G.past0; p < G.past1; p += KV_CHUNK_POS) {
             const int n = min(KV_CHUNK_POS, G.past1 - p);
-            const uint8_t* st = cs.wait(c, 3);
-            if (ci % NCW == cs.warp)
+            if ((int)(cs.seq % NSTAGE) % NCW == cs.warp) {
+                const uint8_t* st = cs.wait(c, 3);
                 chunk(reinterpret_cast<const uint16_t*>(st), reinterpret_cast<const uint16_t*>(st + KV_V_OFFSET), n);
-            cs.release();
+                cs.release_owned();
+            } else {
+                cs.skip();
+            }
         }
-        if (G.owner && ci % NCW == cs.warp) chunk(sm->kvcur[0], sm->kvcur[1], 1);  // the current position
+        if (G.owner && cs.warp == NCW - 1) chunk(sm->kvcur[0], sm->kvcur[1], 1);  // the current position
     }
     // Merge the NCW warp states through shared memory (x is free during attention).
     float* wacc = sm->x;  // [NCW][2][HD]

@@ -52,6 +52,7 @@ struct DecodeParams {
     unsigned long long* trace;      // optional [gridDim.x][trace_slots] globaltimer stamps
     int trace_slots;
     int row_pad;                    // 0: weight rows dense (reference layout); ROW_SKEW: rows padded to rb + ROW_SKEW
+    int kv_pf_pos;                  // cached positions of the next layer's KV each attention split prefetches into L2
 };
 
 // Trace slots: per layer l, stamps at l * TRACE_PER_LAYER + event.

@@ -235,6 +235,7 @@ __device__ void producer_main(const DecodeParams& P, Ctx& c, const Geo& G) {
         }
         // KV rows of this CTA's attention split (positions written by earlier launches).
         if (ok && G.item >= 0) {
+            if (l == 0) pdl_wait();   // cache rows written by the previous step
             const size_t head_off = ((size_t)l * NKVH + G.g) * (size_t)P.max_seq * HD;
             for (int p = G.past0; p < G.past1 && ok; p += KV_CHUNK_POS) {
                 const int n = min(KV_CHUNK_POS, G.past1 - p);
@@ -1218,7 +1219,7 @@ __device__ __forceinline__ void stage_scales(const DecodeParams& P, const Cons& 
 }
 
 template <class WT>
-__device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint32_t epoch, int token,
+__device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint32_t& epoch,
                               unsigned long long& cta_key) {
     constexpr bool L8 = WT::LIMBS;
     Smem* sm = c.sm;
@@ -1231,6 +1232,19 @@ __device__ void consumer_main(const DecodeParams& P, Ctx& c, const Geo& G, uint3
     if (WT::HAS_SCALE) stage_scales(P, cs, G);
     NormW4 w_in, w_post;
     w_in.load(cs, sm->lw[0][LW_IN]);
+    // Everything below reads what the previous step wrote (epoch, input token,
+    // hand-off words, KV cache); everything above reads only weights and tables.
+    pdl_wait();
+    epoch = ld_relaxed32(&P.ws->epoch);
+    int token = P.token_in_dev ? *(volatile const int*)P.token_in_dev : P.token_in;
+    if (token < 0 || token >= VOCAB) {
+        if (cs.tid == 0) {
+            if (cta0) record_error(c, MQ_DEV_BAD_TOKEN, token);
+            sm->abort_flag = 1;
+        }
+        token = 0;
+    }
+    consumers_sync();
     InputScale xin{1.f, 1.f};
     {   // layer-0 input: the embedding row (no exchange)
         uint32_t pay[1][4] = {{0u, 0u, 0u, 0u}};
@@ -1393,10 +1407,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
     Ctx c{sm, P.ws, P.budget_ns};
     if (P.trace && threadIdx.x == 0 && P.L * TRACE_PER_LAYER + 3 < P.trace_slots)   // kernel entry
         P.trace[(size_t)blockIdx.x * P.trace_slots + P.L * TRACE_PER_LAYER + 2] = globaltimer();
+    // Let the next step's grid be scheduled: its CTAs take SMs as this grid's
+    // CTAs exit.  Both griddepcontrol instructions are no-ops for a grid
+    // launched without programmatic stream serialisation.
+    pdl_launch_dependents();
     Geo G;
     G.init(P);
-    const uint32_t epoch = ld_relaxed32(&P.ws->epoch);
-    int token = P.token_in_dev ? *(volatile const int*)P.token_in_dev : P.token_in;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(&sm->full[s], 1);
@@ -1406,19 +1422,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeParams 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (token < 0 || token >= VOCAB) {
-        if (threadIdx.x == 0) {
-            if (G.b == 0) record_error(c, MQ_DEV_BAD_TOKEN, token);
-            sm->abort_flag = 1;
-        }
-        token = 0;
-    }
-    __syncthreads();
     unsigned long long cta_key = 0ull;
+    uint32_t epoch = 0u;
     if (threadIdx.x >= NCT) {
         if (threadIdx.x == NCT) producer_main<WT>(P, c, G);
     } else {
-        consumer_main<WT>(P, c, G, epoch, token, cta_key);
+        consumer_main<WT>(P, c, G, epoch, cta_key);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1544,6 +1553,10 @@ int ensure_smem_attr(DevState& d, int slot, K kernel) {
     if (d.attr_set[slot]) return 0;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
     if (e != cudaSuccess) return (int)e;
+    int per_sm = 0;   // the grid is one CTA per SM: one must fit
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, NTHREADS, sizeof(Smem))) != cudaSuccess)
+        return (int)e;
+    if (per_sm < 1) return MQ_ERR_DEVICE;
     d.attr_set[slot] = true;
     return 0;
 }
@@ -1557,6 +1570,33 @@ int choose_splits(int cache_len, int nb) {
     while (NKVH * s > nb) --s;
     if (s > cache_len) s = cache_len;
     return s < 1 ? 1 : s;
+}
+
+// One decode step is one grid of num_sms CTAs, one per SM (ensure_smem_attr
+// checks that a CTA fits), so on a device without concurrent work every CTA is
+// resident -- the kernel's cross-CTA hand-offs need that; a CTA held back by
+// other work shows up as a bounded-wait timeout (MQ_DEV_TIMEOUT), not a hang.
+// The launch allows programmatic stream serialisation: the next step's CTAs
+// take SMs as this step's CTAs exit and run their read-only prologue (pointer
+// tables, per-row scales, first weight copies) before griddepcontrol.wait.
+// Measured on B200: +1 to +3.5 % tok/s over a cooperative launch, with or
+// without the attribute (a cooperative launch gains nothing from it).  MQ_COOPERATIVE=1
+// selects the plain cooperative launch.
+int g_coop = -1;
+cudaError_t launch_grid(const void* fn, int grid, void** args, size_t smem, cudaStream_t stream) {
+    if (g_coop < 0) g_coop = getenv("MQ_COOPERATIVE") && atoi(getenv("MQ_COOPERATIVE")) ? 1 : 0;
+    if (g_coop) return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NTHREADS), args, smem, stream);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 int launch_step(int kind, DecodeParams& P, cudaStream_t stream) {
@@ -1588,12 +1628,10 @@ int launch_step(int kind, DecodeParams& P, cudaStream_t stream) {
     cudaError_t e;
     if (kind == 0) {
         if ((rc = ensure_smem_attr(*d, 0, decode_kernel<W8>))) return rc;
-        e = cudaLaunchCooperativeKernel((const void*)decode_kernel<W8>, dim3(d->num_sms), dim3(NTHREADS), args,
-                                        sizeof(Smem), stream);
+        e = launch_grid((const void*)decode_kernel<W8>, d->num_sms, args, sizeof(Smem), stream);
     } else {
         if ((rc = ensure_smem_attr(*d, 1, decode_kernel<W16>))) return rc;
-        e = cudaLaunchCooperativeKernel((const void*)decode_kernel<W16>, dim3(d->num_sms), dim3(NTHREADS), args,
-                                        sizeof(Smem), stream);
+        e = launch_grid((const void*)decode_kernel<W16>, d->num_sms, args, sizeof(Smem), stream);
     }
     return (int)e;
 }

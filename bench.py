@@ -10,12 +10,16 @@ every step streams them from HBM; no extra flush is needed.
           token feedback (mq_decode_multi), CUDA events on the launching stream.
   e2e     the same tokens/s through the reference-facing call
           A10Int8MegakernelDecoder.decode_step(token) -> int, which passes the
-          token to the kernel and reads the argmax back with .item() every step.
+          token to the kernel and reads the argmax back into host memory every
+          step (the kernel writes it into pinned memory; stream synchronise).
   --impl reference   the reference's PyTorch formulation of the same math
           (oracle/oracle.py, a CPU restatement of int8_decoder.py:263-298 with
           INT8 on every projection) timed on the host cores.
-Multi-GPU (torchrun): batch-1 decode does not shard, so every rank runs an
-independent replica; value = all ranks' tokens / max over ranks of the time.
+Multi-GPU (torchrun): the line is config 4 (batched decode, 64 sequences per
+GPU) unless --config says otherwise; every rank runs an independent replica (no
+collective on the data path); value = all ranks' tokens / max over ranks of
+the CUDA-event time.  --config 0/2/3 and --prefill select the other BASELINE
+configs on one GPU.
 """
 import argparse
 import json

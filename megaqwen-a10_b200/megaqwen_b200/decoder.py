@@ -106,6 +106,9 @@ class _MegakernelDecoderBase:
         self.position_ = 0
         self.attn_scale_ = 1.0 / (HEAD_DIM ** 0.5)
         _lib.load()
+        # A decode step reads weights and pointer tables before its dependency
+        # wait on the previous kernel: finish writing them here.
+        torch.cuda.synchronize(dev)
 
     def _padded(self, t):
         extra = _lib.ROW_PAD // t.element_size()
